@@ -1,0 +1,114 @@
+/*
+ * nibblegemm_b200 -- C ABI of the B200 (sm_100a) W4A16 kernel library.
+ *
+ * Packed format (identical to arvindcr4/nibblegemm, python/nibblegemm/quant.py:8-54):
+ *   qweight  int32 [K/8, N]: eight 4-bit codes along K per word, logical k of
+ *            the word stored in nibble slot (k odd ? 4 + k/2 : k/2), i.e. slot
+ *            order 0,4,1,5,2,6,3,7; code u means (u - 8) * scale.
+ *   scales   fp16  [K/G, N]: one scale per (group of G rows of K, column).
+ *   x        fp16 or bf16 [M, K] row-major;  y same dtype as x, [M, N].
+ *   Y = X @ W with W[k, n] = (u[k, n] - 8) * scales[k / G, n].
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers, caller-owned, contiguous row-major.
+ *     The library allocates nothing and never synchronises (except
+ *     ng_device_status); work is enqueued on `stream` (a cudaStream_t;
+ *     NULL = legacy default stream) of the current device.
+ *   - Return value: NG_OK (0) or a positive NG_ERR_* status; nothing aborts.
+ *     ng_status_string() names the status.  Validation happens before any
+ *     launch, so a non-zero status from validation enqueues nothing.
+ *   - Calls are thread-safe; the only library state is a per-device cache of
+ *     device properties and kernel attributes, initialised on first use, and
+ *     a per-device error word that kernels set when a bounded wait expires.
+ */
+#ifndef NIBBLEGEMM_B200_H
+#define NIBBLEGEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define NG_OK 0
+#define NG_ERR_NULL_POINTER 1       /* a required pointer is NULL                     */
+#define NG_ERR_BAD_DTYPE 2          /* dtype code not NG_DTYPE_F16 / NG_DTYPE_BF16     */
+#define NG_ERR_BAD_SHAPE 3          /* M, K, N or group size inconsistent/unsupported  */
+#define NG_ERR_MISALIGNED 4         /* a pointer lacks the alignment its loads need    */
+#define NG_ERR_BAD_ARGUMENT 5       /* an option (splits, threads, algo, tile) out of range */
+#define NG_ERR_LAUNCH 6             /* the CUDA launch itself failed                   */
+#define NG_ERR_UNSUPPORTED_DEVICE 7 /* current device is not sm_100                    */
+#define NG_ERR_CUDA 8               /* another CUDA runtime/driver call failed         */
+#define NG_ERR_DEVICE_TIMEOUT 9     /* a kernel's bounded pipeline wait expired        */
+
+/* Activation / output element types. */
+#define NG_DTYPE_F16 0
+#define NG_DTYPE_BF16 1
+
+/* Library ABI version (bumped on any signature change). */
+int ng_abi_version(void);
+
+/* Human-readable name of a status code (static storage, never NULL). */
+const char* ng_status_string(int status);
+
+/*
+ * Synchronise `stream`, then return NG_ERR_DEVICE_TIMEOUT if any kernel of this
+ * library on the current device gave up on a bounded wait since the last call
+ * (and clear that flag), NG_ERR_CUDA if the stream reports an error, else NG_OK.
+ * No counterpart in the reference (its kernels have no waits that can expire).
+ */
+int ng_device_status(void* stream);
+
+/*
+ * Dense dequantisation: out[K, N] = (u - 8) * scale, one rounding to out_dtype.
+ * Replaces the reference's `dequant_w4(Wq, S, group_size, fast)`
+ * (csrc/dequant_kernel.cu:48-74, bound at csrc/bindings.cpp:19-20).
+ *   fast != 0 : lop3 / magic-number decode;  fast == 0 : shift-mask-convert decode.
+ *   Both are bit-exact with the CPU oracle for NG_DTYPE_F16 (the reference's
+ *   only output type); NG_DTYPE_BF16 rounds the same exact product to bf16.
+ *   Requires K % 8 == 0, K % group_size == 0, group_size % 8 == 0, N >= 1.
+ */
+int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int out_dtype,
+                  int K, int N, int group_size, int fast, void* stream);
+
+/*
+ * Decode-regime fused dequant GEMV, one launch (split-K partials are reduced
+ * across the CTAs of a thread-block cluster through distributed shared memory,
+ * in fixed rank order, so results are deterministic and no workspace is needed).
+ * Replaces the reference's `gemv_w4a16(X, Wq, S, group_size, version,
+ * splits_override, threads_override)` (csrc/gemv_w4a16.cu:341-425, bound at
+ * csrc/bindings.cpp:12-15).
+ *   M in [1, 16]; N % 4 == 0; group_size in {64, 128, 256}; K % group_size == 0.
+ *   splits: number of K slices (cluster size), 0 = heuristic, else 1..16.
+ *   block_threads: 0 = heuristic (256), else 128 or 256.
+ *   algo: 0 = default for the dtype; 1 = fp16 magic decode with packed-half2
+ *         FMA windows of 32 values flushed to fp32 (fp16 x only);
+ *         2 = fp32 magic decode with packed fp32x2 FMA, fp32 throughout.
+ *         Default: 1 for fp16 x, 2 for bf16 x.
+ *   x 16-byte aligned; qweight 16-byte aligned; scales 8-byte aligned.
+ */
+int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
+                  void* y, int M, int K, int N, int group_size, int splits, int block_threads,
+                  int algo, void* stream);
+
+/*
+ * Prefill-regime fused dequant GEMM on the sm_100 tensor cores: tcgen05.mma
+ * with accumulators in tensor memory, activations staged by TMA, weight tiles
+ * decoded by CUDA-core warps straight into the tensor cores' shared-memory
+ * layout.  Persistent, warp-specialised, one launch.
+ * Replaces the reference's `gemm_w4a16(X, Wq, S, group_size, version)`
+ * (csrc/gemm_w4a16.cu:379-429, bound at csrc/bindings.cpp:16-18).
+ *   Any M >= 1; K % 64 == 0; N % 4 == 0; group_size in {64, 128, 256};
+ *   x, qweight 16-byte aligned; scales 2-byte aligned.
+ *   tile_tokens: 0 = heuristic, else 16, 32, 64, 128 or 256 rows of X per tile.
+ */
+int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
+                  void* y, int M, int K, int N, int group_size, int tile_tokens, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NIBBLEGEMM_B200_H */

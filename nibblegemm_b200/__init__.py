@@ -1,0 +1,24 @@
+"""nibblegemm_b200 -- W4A16 (packed INT4 weight, fp16/bf16 activation) kernels for B200.
+
+A drop-in for the hot path of arvindcr4/nibblegemm: the same packed format, the
+same ops (``gemv_w4a16`` / ``gemm_w4a16`` / ``dequant_w4`` via ``extension()``),
+the same Python names, the same ``QuantLinear`` -- with hand-written sm_100a
+kernels behind a C ABI (``include/nibblegemm_b200.h``).
+"""
+from .ops import DECODE_MAX_M, QuantLinear, dequant, extension, gemm, gemv, matmul
+from .quant import QuantizedWeight, pack_nibbles, quantize, unpack_nibbles
+
+__all__ = [
+    "DECODE_MAX_M",
+    "QuantLinear",
+    "QuantizedWeight",
+    "dequant",
+    "extension",
+    "gemm",
+    "gemv",
+    "matmul",
+    "pack_nibbles",
+    "quantize",
+    "unpack_nibbles",
+]
+__version__ = "0.1.0"

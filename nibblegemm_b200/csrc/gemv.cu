@@ -1,0 +1,376 @@
+// Decode-regime fused dequant GEMV: Y[M, N] = X[M, K] @ W, M <= 16, one launch.
+//
+// Work decomposition (all sizes in packed rows: one packed row = 8 values of K)
+//   * A CTA owns a 128-column tile (32 lanes x 4 columns, one 16-byte packed
+//     load per lane per row) and a contiguous K slice of `rows_per_cta` rows.
+//   * The CTAs sharing a column tile form one thread-block cluster along
+//     gridDim.y (cluster size = number of K slices, up to 16).  Each CTA reduces
+//     its warps' partial sums in shared memory, then the cluster reduces the
+//     slices through distributed shared memory: CTA r of the cluster sums a
+//     1/C share of the tile's outputs over ranks 0..C-1 in fixed order and
+//     writes them.  No global workspace, no second launch, deterministic.
+//   * Inside a CTA, warps take 8-row chunks (64 values of K, always inside one
+//     quantisation group because G >= 64) round-robin.  A chunk issues its eight
+//     16-byte weight loads back to back before decoding any of them, so every
+//     lane keeps 128 bytes in flight; at 2-4 resident CTAs of 8 warps per SM
+//     that is 64-128 KB per SM, comfortably above the bandwidth-latency product.
+//   * Activations for the CTA's K slice are staged once in shared memory (in
+//     the accumulation type) and read as broadcasts.
+//
+// Two accumulation paths:
+//   * kHalf2 (fp16 activations): the fp16 magic-number decode, packed half2
+//     FMA over 32 values of K, then a flush into fp32 multiplied by the group
+//     scale.  9 decode instructions + 4 HFMA2 per word per row of X.
+//   * kFloat2 (bf16 activations; optional for fp16): the fp32 magic-number
+//     decode (exact u - 8 as fp32x2 pairs) and packed fp32x2 FMA, scale applied
+//     once per 8-row chunk (or per word for M >= 8, to bound registers).
+//     Accumulation is fp32 throughout.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+#include "ng_decode.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace ngb {
+namespace {
+
+constexpr int kCols = 128;  // columns per CTA tile
+constexpr int kU = 8;       // packed rows per chunk
+constexpr int kWin = 4;     // half2 path: packed rows per fp16 accumulation window
+constexpr int kMaxCluster = 16;
+constexpr int kStageBytes = 32 * 1024;  // activation staging budget per slab
+
+enum Path { kHalf2 = 0, kFloat2 = 1 };
+
+template <int MT, bool XBF16, int PATH, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+    gemv_kernel(const void* __restrict__ x, const uint32_t* __restrict__ qw,
+                const __half* __restrict__ scales, void* __restrict__ y, int M, int K, int N,
+                int G, int rows_per_cta, int slab_rows, int csize) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  using XS = typename std::conditional<PATH == kFloat2, float, __half>::type;
+  XS* xs = reinterpret_cast<XS*>(smem);
+  const int xstride = slab_rows * 8;  // staged elements per row of X
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int krows = K >> 3;
+  const int kr0 = blockIdx.y * rows_per_cta;
+  const int kr1 = min(krows, kr0 + rows_per_cta);
+  const int col = blockIdx.x * kCols + lane * 4;
+  const bool col_ok = col < N;
+  const uint64_t pol = make_evict_first_policy();
+  const unsigned short* xin = static_cast<const unsigned short*>(x);
+
+  float acc[4][MT];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[c][m] = 0.f;
+
+  for (int s0 = kr0; s0 < kr1; s0 += slab_rows) {
+    const int nrows = min(slab_rows, kr1 - s0);
+    __syncthreads();  // previous slab fully consumed
+    // ---- stage X[:, s0*8 : (s0+nrows)*8) -------------------------------------
+    for (int i = tid; i < MT * nrows; i += WARPS * 32) {
+      const int m = i / nrows;
+      const int r = i - m * nrows;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (m < M) v = ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(s0 + r) * 8);
+      XS* dst = xs + m * xstride + r * 8;
+      if constexpr (PATH == kFloat2) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (XBF16) {
+            f[2 * j] = __uint_as_float(w[j] << 16);
+            f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+          } else {
+            const float2 t = __half22float2(h2_from_bits(w[j]));
+            f[2 * j] = t.x;
+            f[2 * j + 1] = t.y;
+          }
+        }
+        reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
+    }
+    __syncthreads();
+
+    // ---- stream the weights ---------------------------------------------------
+    const int nch = nrows / kU;
+    for (int ch = warp; ch < nch; ch += WARPS) {
+      const int r0 = s0 + ch * kU;
+      uint4 q[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        q[u] = col_ok ? ld_stream_v4(qw + static_cast<size_t>(r0 + u) * N + col, pol)
+                      : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+      const int grp = (r0 * 8) / G;
+      const uint2 sv = col_ok ? ld_ro_v2(scales + static_cast<size_t>(grp) * N + col)
+                              : make_uint2(0u, 0u);
+      float sc[4];
+      sc[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFF)));
+      sc[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
+      sc[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFF)));
+      sc[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
+      const XS* xc = xs + (r0 - s0) * 8;
+
+      if constexpr (PATH == kHalf2) {
+#pragma unroll
+        for (int win = 0; win < kU / kWin; ++win) {
+          __half2 h[4][MT];
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) h[c][m] = __float2half2_rn(0.f);
+#pragma unroll
+          for (int rr = 0; rr < kWin; ++rr) {
+            const int u = win * kWin + rr;
+            const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+            __half2 wv[4][4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) decode8_f16(words[c], wv[c]);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(xc + m * xstride + u * 8);
+              const __half2 xh[4] = {h2_from_bits(xv.x), h2_from_bits(xv.y), h2_from_bits(xv.z),
+                                     h2_from_bits(xv.w)};
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) h[c][m] = __hfma2(wv[c][i], xh[i], h[c][m]);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              const float2 f = __half22float2(h[c][m]);
+              acc[c][m] = fmaf(f.x + f.y, sc[c], acc[c][m]);
+            }
+        }
+      } else {
+        constexpr bool kScaleEarly = MT >= 8;
+        f2 a2[4][MT];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) a2[c][m] = f2_make(0.f, 0.f);
+        f2 s2[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s2[c] = f2_make(sc[c], sc[c]);
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+          f2 wv[4][4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t w16 = words[c] >> 16;
+            wv[c][0] = decode_pair_f32<0>(words[c], w16);
+            wv[c][1] = decode_pair_f32<1>(words[c], w16);
+            wv[c][2] = decode_pair_f32<2>(words[c], w16);
+            wv[c][3] = decode_pair_f32<3>(words[c], w16);
+            if constexpr (kScaleEarly) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) wv[c][j] = f2_mul(wv[c][j], s2[c]);
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const float4 xa = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8);
+            const float4 xb = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8 + 4);
+            const f2 xp[4] = {f2_make(xa.x, xa.y), f2_make(xa.z, xa.w), f2_make(xb.x, xb.y),
+                              f2_make(xb.z, xb.w)};
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) a2[c][m] = f2_fma(wv[c][j], xp[j], a2[c][m]);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float lo, hi;
+            f2_split(a2[c][m], lo, hi);
+            if constexpr (kScaleEarly)
+              acc[c][m] += lo + hi;
+            else
+              acc[c][m] = fmaf(lo + hi, sc[c], acc[c][m]);
+          }
+      }
+    }
+  }
+
+  // ---- CTA reduction over warps (fixed order) ---------------------------------
+  constexpr int E = MT * kCols;
+  const size_t stage_bytes = static_cast<size_t>(MT) * xstride * sizeof(XS);
+  const size_t red_bytes = static_cast<size_t>(WARPS) * E * sizeof(float);
+  float* red = reinterpret_cast<float*>(smem);
+  float* fin = reinterpret_cast<float*>(smem + (stage_bytes > red_bytes ? stage_bytes : red_bytes));
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+    *reinterpret_cast<float4*>(red + (warp * MT + m) * kCols + lane * 4) =
+        make_float4(acc[0][m], acc[1][m], acc[2][m], acc[3][m]);
+  __syncthreads();
+
+  auto store = [&](int e, float v) {
+    const int m = e / kCols;
+    const int cn = blockIdx.x * kCols + (e % kCols);
+    if (m < M && cn < N) {
+      unsigned short* yo = static_cast<unsigned short*>(y);
+      yo[static_cast<size_t>(m) * N + cn] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                  : __half_as_ushort(__float2half_rn(v));
+    }
+  };
+
+  if (csize == 1) {
+    for (int e = tid; e < E; e += WARPS * 32) {
+      float v = 0.f;
+#pragma unroll 4
+      for (int w = 0; w < WARPS; ++w) v += red[w * E + e];
+      store(e, v);
+    }
+    return;
+  }
+  for (int e = tid; e < E; e += WARPS * 32) {
+    float v = 0.f;
+#pragma unroll 4
+    for (int w = 0; w < WARPS; ++w) v += red[w * E + e];
+    fin[e] = v;
+  }
+  // ---- cluster reduction over K slices through DSMEM ---------------------------
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int per = (E + csize - 1) / csize;
+  const int e0 = rank * per;
+  const int e1 = min(E, e0 + per);
+  for (int e = e0 + tid; e < e1; e += WARPS * 32) {
+    float v = 0.f;
+    for (int r = 0; r < csize; ++r) v += cluster.map_shared_rank(fin, r)[e];
+    store(e, v);
+  }
+  cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+template <int MT, bool XBF16, int PATH, int WARPS>
+int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N, int G,
+        int splits, const DeviceInfo& dev, cudaStream_t stream) {
+  auto kern = gemv_kernel<MT, XBF16, PATH, WARPS>;
+  constexpr int threads = WARPS * 32;
+  constexpr int esz = PATH == kFloat2 ? 4 : 2;
+  const int krows = K / 8;
+  const int col_tiles = (N + kCols - 1) / kCols;
+
+  // Per-device one-time attribute set-up for this instantiation.
+  static std::once_flag once[64];
+  static int occ_cache[64];
+  const int d = dev.device;
+  std::call_once(once[d], [&] {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    int occ = 0;
+    const size_t probe_smem = static_cast<size_t>(WARPS) * MT * kCols * 4 * 2;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, probe_smem) != cudaSuccess)
+      occ = 1;
+    occ_cache[d] = std::max(1, occ);
+  });
+
+  int C;
+  if (splits > 0) {
+    C = splits;
+  } else {
+    const int target = dev.sm_count * occ_cache[d];
+    C = std::max(1, target / std::max(1, col_tiles));
+  }
+  C = std::min(C, kMaxCluster);
+  C = std::max(1, std::min(C, krows / kU));
+  int rows_per_cta = (krows + C - 1) / C;
+  rows_per_cta = (rows_per_cta + kU - 1) / kU * kU;
+  C = (krows + rows_per_cta - 1) / rows_per_cta;  // trim empty slices
+
+  int slab_max = kStageBytes / (MT * 8 * esz);
+  slab_max = std::max(kU, slab_max / kU * kU);
+  const int slab_rows = std::min(rows_per_cta, slab_max);
+  const size_t stage = static_cast<size_t>(MT) * slab_rows * 8 * esz;
+  const size_t red = static_cast<size_t>(WARPS) * MT * kCols * 4;
+  const size_t smem = std::max(stage, red) + static_cast<size_t>(MT) * kCols * 4;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(col_tiles, C, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = C;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return launch_status(
+      cudaLaunchKernelEx(&cfg, kern, x, qw, s, y, M, K, N, G, rows_per_cta, slab_rows, C));
+}
+
+template <bool XBF16, int PATH, int WARPS>
+int dispatch_m(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N,
+               int G, int splits, const DeviceInfo& dev, cudaStream_t st) {
+  if (M <= 1) return run<1, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 2) return run<2, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 4) return run<4, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 8) return run<8, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  return run<16, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
+}
+
+template <bool XBF16, int PATH>
+int dispatch_w(int threads, const void* x, const uint32_t* qw, const __half* s, void* y, int M,
+               int K, int N, int G, int splits, const DeviceInfo& dev, cudaStream_t st) {
+  if (threads == 128) return dispatch_m<XBF16, PATH, 4>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  return dispatch_m<XBF16, PATH, 8>(x, qw, s, y, M, K, N, G, splits, dev, st);
+}
+
+}  // namespace
+}  // namespace ngb
+
+extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
+                             const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                             int splits, int block_threads, int algo, void* stream) {
+  using namespace ngb;
+  if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
+  if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
+  if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
+  if (algo < 0 || algo > 2) return NG_ERR_BAD_ARGUMENT;
+  if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
+  const int threads = block_threads ? block_threads : 256;
+  if (x_dtype == NG_DTYPE_BF16)
+    return dispatch_w<true, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
+  if (algo == 2)
+    return dispatch_w<false, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
+  return dispatch_w<false, kHalf2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
+}

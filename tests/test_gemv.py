@@ -1,0 +1,137 @@
+"""Parity of the decode GEMV (``gemv_w4a16``) with the CPU oracle.
+
+Gate: max|y - ref| / max|ref| <= 5e-3 against the oracle's fp32 result, where
+ref = X @ dequant(W) with the reference's fp16-rounded weights (quant.py:207-215).
+Expected error, derived per path:
+  * algo 1 (fp16 activations): half2 accumulation of 16 products per lane per
+    32-value window, then fp32.  CPU emulation of this scheme on config 1 gives
+    ~7e-4; the fp16 output rounding alone is 2**-11 ~ 4.9e-4 of max|ref|.
+  * algo 2 / bf16: exact fp32 weights and fp32 accumulation: only summation
+    order (~1e-6) and the output rounding (fp16 4.9e-4, bf16 3.9e-3 of max|ref|).
+The reference suite's own metric (max|err| / mean|ref| < 5e-2, tests/test_gemv.py)
+is checked as well.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import nibblegemm_b200 as ng
+from oracle import c_oracle
+from oracle import quant_oracle as qo
+from tests.conftest import max_rel, mean_rel
+
+pytestmark = pytest.mark.gpu
+
+GATE = 5e-3
+REF_TOL = 5e-2
+
+
+def make_case(M, K, N, G=128, seed=0, act="f16"):
+    x, q, s = qo.synthetic_case(M, K, N, group_size=G, seed=seed, act=act)
+    qw = ng.QuantizedWeight(torch.from_numpy(q), torch.from_numpy(s), G, K, N).to("cuda")
+    if act == "f16":
+        X = torch.from_numpy(x).cuda()
+        ref = c_oracle.matmul_f32(x, q, s, G, K)
+    else:
+        X = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda()
+        ref = c_oracle.matmul_f32(x, q, s, G, K, x_kind="bf16")
+    return X, qw, ref
+
+
+def check(y, ref, dtype):
+    assert y.dtype == dtype
+    yf = y.float().cpu().numpy()
+    assert np.isfinite(yf).all()
+    err = max_rel(yf, ref)
+    assert err <= GATE, err
+    assert mean_rel(yf, ref) < REF_TOL
+    return err
+
+
+CASES = [(1, 512, 256), (2, 256, 132), (3, 1024, 260), (4, 512, 512), (5, 2048, 132),
+         (8, 512, 256), (9, 1024, 388), (13, 256, 128), (16, 512, 1028)]
+
+
+@pytest.mark.parametrize("M,K,N", CASES)
+@pytest.mark.parametrize("G", [64, 128])
+@pytest.mark.parametrize("act,algo", [("f16", 1), ("f16", 2), ("bf16", 0)])
+def test_gemv_matches_oracle(M, K, N, G, act, algo):
+    X, qw, ref = make_case(M, K, N, G, seed=M * 7 + N, act=act)
+    y = ng.gemv(X, qw, algo=algo)
+    assert y.shape == (M, N)
+    check(y, ref, X.dtype)
+
+
+@pytest.mark.parametrize("M", [1, 4, 8, 16])
+@pytest.mark.parametrize("splits", [1, 2, 4, 5, 16])
+@pytest.mark.parametrize("threads", [128, 256])
+def test_split_and_block_invariance(M, splits, threads):
+    """Any K split / block width gives the same answer to fp32 summation order."""
+    X, qw, ref = make_case(M, 1024, 256, 64, seed=2)
+    y = ng.gemv(X, qw, splits=splits, block_threads=threads)
+    check(y, ref, torch.float16)
+    base = ng.gemv(X, qw, splits=1, block_threads=256)
+    d = (y.float() - base.float()).abs().max().item() / base.float().abs().max().item()
+    assert d < 2e-3
+
+
+def test_version3_is_one_split():
+    X, qw, _ = make_case(4, 1024, 256, 64, seed=3)
+    assert torch.equal(ng.gemv(X, qw, version=4, splits=1), ng.gemv(X, qw, version=3))
+
+
+def test_deterministic():
+    X, qw, _ = make_case(4, 4096, 1024, 128, seed=4)
+    a = ng.gemv(X, qw)
+    for _ in range(3):
+        assert torch.equal(a, ng.gemv(X, qw))
+
+
+def test_rejects_m_above_16():
+    X, qw, _ = make_case(17, 256, 132, 128, seed=5)
+    with pytest.raises(RuntimeError):
+        ng.gemv(X, qw)
+
+
+def test_rejects_bad_inputs():
+    X, qw, _ = make_case(2, 256, 132, 128, seed=6)
+    with pytest.raises(RuntimeError):
+        ng.gemv(X.float(), qw)
+    with pytest.raises(RuntimeError):
+        ng.gemv(X[:, :128], qw)
+
+
+def test_matmul_dispatch_and_k_mismatch():
+    X, qw, _ = make_case(ng.DECODE_MAX_M, 512, 256, 128, seed=7)
+    assert torch.equal(ng.matmul(X, qw), ng.gemv(X, qw, version=4))
+    with pytest.raises(ValueError):
+        ng.matmul(torch.randn(1, 256, device="cuda", dtype=torch.float16), qw)
+
+
+def test_output_fully_written():
+    """A poisoned output buffer must be completely overwritten."""
+    X, qw, ref = make_case(3, 1024, 1028, 128, seed=8)
+    out = torch.full((3, 1028), float("nan"), dtype=torch.float16, device="cuda")
+    ng.extension().gemv_w4a16(X, qw.qweight, qw.scales, 128, out=out)
+    check(out, ref, torch.float16)
+
+
+# BASELINE config 1 and the config 2 sweep shapes at full size.
+FULL = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096), (8192, 8192)]
+
+
+@pytest.mark.parametrize("K,N", FULL)
+@pytest.mark.parametrize("M", [1, 16])
+def test_full_size_shapes(K, N, M):
+    X, qw, ref = make_case(M, K, N, 128, seed=K + N + M)
+    check(ng.gemv(X, qw), ref, torch.float16)
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
+def test_config1_bf16_and_fp32_path(M):
+    X, qw, ref = make_case(M, 4096, 14336, 128, seed=11, act="bf16")
+    check(ng.gemv(X, qw), ref, torch.bfloat16)
+    X, qw, ref = make_case(M, 4096, 14336, 128, seed=12)
+    check(ng.gemv(X, qw, algo=2), ref, torch.float16)
