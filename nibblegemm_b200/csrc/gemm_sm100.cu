@@ -1,7 +1,383 @@
-// Placeholder until the tcgen05 GEMM lands.
-#include "ng_common.cuh"
-extern "C" int ng_gemm_w4a16(const void* x, int, const int32_t* q, const uint16_t* s, void* y, int,
-                             int, int, int, int, void*) {
-  if (!x || !q || !s || !y) return NG_ERR_NULL_POINTER;
-  return NG_ERR_BAD_ARGUMENT;
+// Prefill-regime fused dequant GEMM on the sm_100 tensor cores.
+//
+// Y[M, N] = X[M, K] @ W.  The product is computed transposed, Y^T = W^T X^T,
+// so that the *weights* are the MMA's 128-row A operand and the activations
+// are its N operand (BT = 16..256 rows of X per tile):
+//   * a tile is 128 output columns (n) x BT rows of X (tokens); its fp32
+//     accumulator is a 128-lane x BT-column block of tensor memory;
+//   * each decoded weight (one value of W) feeds 2*BT flops, twice what a
+//     128-token x 256-column tile of the untransposed product would get, so the
+//     CUDA-core decode needed per tensor-core flop is halved;
+//   * small batches (M = 16 .. 128) use a narrow N side instead of padding a
+//     128-row M side.
+//
+// Warp roles (384 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer: packed weight tile [8 words x 128 columns] and
+//               the X tile [BT rows x 64 values, 128-byte swizzle] per k-step
+//   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16 each) per k-step, commit
+//               to the stage's "empty" barrier; per tile, commit to "acc full"
+//   warp 2      tensor-memory allocator (2 x BT columns: double-buffered acc)
+//   warps 4-7   epilogue: tcgen05.ld 128 lanes x BT columns -> fp16/bf16 -> Y
+//   warps 8-11  dequant: thread t owns weight column n0 + t; per k-step it
+//               decodes 8 packed words (64 values of K) with the magic-number
+//               method, applies the group scale (one rounding, so the fp16
+//               operand equals the reference's dequantised weight bit for
+//               bit), and writes one 128-byte row of the A tile in the
+//               tensor cores' 128-byte-swizzled K-major layout.
+// Pipelines: S stages of {A 16 KB, X BT*128 B, raw 4 KB} guarded by
+// full (TMA tx) / afull (dequant) / empty (MMA commit) mbarriers; two
+// accumulator buffers guarded by tfull / tempty.  Every wait is bounded.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "ng_decode.cuh"
+#include "sm100_primitives.cuh"
+
+namespace ngb {
+namespace {
+
+constexpr int kTileN = 128;        // weight columns per tile (MMA M)
+constexpr int kBK = 64;            // values of K per k-step (one 128-byte swizzle row)
+constexpr int kThreads = 384;
+constexpr int kATileBytes = kTileN * kBK * 2;   // 16 KB decoded weights
+constexpr int kRawBytes = (kBK / 8) * kTileN * 4;  // 4 KB packed words
+constexpr int kSmemBudget = 220 * 1024;
+
+struct Barriers {
+  uint64_t full[16];
+  uint64_t afull[16];
+  uint64_t empty[16];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+template <int BT, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                const __grid_constant__ CUtensorMap tmap_q, const __half* __restrict__ scales,
+                void* __restrict__ y, int M, int K, int N, int G, int stages,
+                unsigned int* __restrict__ err) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // 1024-byte alignment for the swizzled operand tiles.
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int kBTileBytes = BT * kBK * 2;
+  constexpr int kStageBytes = kATileBytes + kBTileBytes + kRawBytes;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + stages * kStageBytes);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tiles = (N + kTileN - 1) / kTileN;
+  const int m_tiles = (M + BT - 1) / BT;
+  const int tiles = n_tiles * m_tiles;
+  const int kb_count = K / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->afull[s], 4);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->tfull[a], 1);
+      mbar_init(&bars->tempty[a], 4);
+    }
+    bars->abort = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_q);
+  }
+  if (warp == 2) tmem_alloc(&bars->tmem_slot, 2 * BT);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles) * kTileN;
+        const int m0 = (tile / n_tiles) * BT;
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t ph = (it / stages) & 1;
+          if (!mbar_wait_bounded(&bars->empty[s], ph ^ 1, err, abort)) break;
+          unsigned char* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kBTileBytes + kRawBytes);
+          tma_load_2d(st + kATileBytes + kBTileBytes, &tmap_q, &bars->full[s], n0, kb * (kBK / 8));
+          tma_load_2d(st + kATileBytes, &tmap_x, &bars->full[s], kb * kBK, m0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(BF16, kTileN, BT);
+      int it = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        const uint32_t aph = (lt >> 1) & 1;
+        if (!mbar_wait_bounded(&bars->tempty[acc], aph ^ 1, err, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BT;
+        bool ok = true;
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t ph = (it / stages) & 1;
+          if (!mbar_wait_bounded(&bars->full[s], ph, err, abort) ||
+              !mbar_wait_bounded(&bars->afull[s], ph, err, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * kStageBytes);
+          const uint32_t b_addr = a_addr + kATileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // Advancing 16 values (32 bytes) along K inside the swizzle atom
+            // is a plain start-address offset: the hardware applies the XOR
+            // pattern to the absolute address bits.
+            umma_f16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32),
+                     idesc, (kb | kk) != 0);
+          }
+          umma_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bars->tfull[acc]);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - 4;  // TMEM lanes 32e .. 32e+31
+    int lt = 0;
+    unsigned short* yo = static_cast<unsigned short*>(y);
+    for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, ++lt) {
+      const int n0 = (tile % n_tiles) * kTileN;
+      const int m0 = (tile / n_tiles) * BT;
+      const int acc = lt & 1;
+      const uint32_t aph = (lt >> 1) & 1;
+      if (!mbar_wait_bounded(&bars->tfull[acc], aph, err, abort)) break;
+      tc_fence_after();
+      const int n = n0 + e * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(e * 32) << 16) + acc * BT;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BT; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld_16(taddr + c0, r);
+        tmem_ld_wait();
+        if (n < N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < M) {
+              const float v = __uint_as_float(r[j]);
+              yo[static_cast<size_t>(m) * N + n] = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                        : __half_as_ushort(__float2half_rn(v));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dequant
+    const int t = threadIdx.x - 256;  // weight column within the tile
+    const int atom = t >> 3, r8 = t & 7;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+      const int n = (tile % n_tiles) * kTileN + t;
+      const bool n_ok = n < N;
+      bool ok = true;
+      for (int kb = 0; kb < kb_count; ++kb, ++it) {
+        const int s = it % stages;
+        const uint32_t ph = (it / stages) & 1;
+        const int g = (kb * kBK) / G;
+        const __half sc = n_ok ? scales[static_cast<size_t>(g) * N + n] : __float2half(0.f);
+        if (!mbar_wait_bounded(&bars->full[s], ph, err, abort)) {
+          ok = false;
+          break;
+        }
+        unsigned char* st = smem + s * kStageBytes;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + kBTileBytes);
+        unsigned char* arow = st + atom * 1024 + r8 * 128;
+#pragma unroll
+        for (int r = 0; r < kBK / 8; ++r) {
+          const uint32_t q = raw[r * kTileN + t];
+          uint4 v;
+          if constexpr (!BF16) {
+            __half2 w[4];
+            decode8_f16(q, w);
+            const __half2 s2 = __half2half2(sc);
+            v.x = h2_bits(__hmul2(w[0], s2));
+            v.y = h2_bits(__hmul2(w[1], s2));
+            v.z = h2_bits(__hmul2(w[2], s2));
+            v.w = h2_bits(__hmul2(w[3], s2));
+          } else {
+            const uint32_t q16 = q >> 16;
+            const float sf = __half2float(sc);
+            const f2 s2 = f2_make(sf, sf);
+            const f2 p[4] = {decode_pair_f32<0>(q, q16), decode_pair_f32<1>(q, q16),
+                             decode_pair_f32<2>(q, q16), decode_pair_f32<3>(q, q16)};
+            uint32_t b[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float lo, hi;
+              f2_split(f2_mul(p[j], s2), lo, hi);
+              const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
+              b[j] = *reinterpret_cast<const uint32_t*>(&bb);
+            }
+            v = make_uint4(b[0], b[1], b[2], b[3]);
+          }
+          *reinterpret_cast<uint4*>(arow + ((r ^ r8) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->afull[s]);
+      }
+      if (!ok) break;
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {
+    // Let any TMA copy still in flight land before the CTA's shared memory is
+    // released (bounded: copies complete in microseconds).
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 200000ull) {
+    }
+  }
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BT);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_maps(const void* x, const int32_t* q, int M, int K, int N, int BT, CUtensorMap* mx,
+              CUtensorMap* mq) {
+  auto enc = encode_fn();
+  if (!enc) return NG_ERR_CUDA;
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(BT)};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(mx, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(x), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return NG_ERR_CUDA;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K / 8)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileN), static_cast<cuuint32_t>(kBK / 8)};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(mq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<int32_t*>(q), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return NG_ERR_CUDA;
+  }
+  return NG_OK;
+}
+
+template <int BT, bool BF16>
+int run_gemm(const void* x, const int32_t* q, const __half* s, void* y, int M, int K, int N, int G,
+             const DeviceInfo& dev, cudaStream_t stream) {
+  CUtensorMap mx, mq;
+  if (int st = make_maps(x, q, M, K, N, BT, &mx, &mq)) return st;
+  constexpr int stage_bytes = kATileBytes + BT * kBK * 2 + kRawBytes;
+  int stages = std::min(16, (kSmemBudget - 1024 - static_cast<int>(sizeof(Barriers))) / stage_bytes);
+  const size_t smem = 1024 + static_cast<size_t>(stages) * stage_bytes + sizeof(Barriers);
+  auto kern = gemm_kernel<BT, BF16>;
+  static std::once_flag once[64];
+  std::call_once(once[dev.device], [&] {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 4096);
+  });
+  const int tiles = ((N + kTileN - 1) / kTileN) * ((M + BT - 1) / BT);
+  const int grid = std::min(tiles, dev.sm_count);
+  kern<<<grid, kThreads, smem, stream>>>(mx, mq, s, y, M, K, N, G, stages, dev.err);
+  return launch_status();
+}
+
+template <bool BF16>
+int dispatch_bt(int bt, const void* x, const int32_t* q, const __half* s, void* y, int M, int K,
+                int N, int G, const DeviceInfo& dev, cudaStream_t st) {
+  switch (bt) {
+    case 16: return run_gemm<16, BF16>(x, q, s, y, M, K, N, G, dev, st);
+    case 32: return run_gemm<32, BF16>(x, q, s, y, M, K, N, G, dev, st);
+    case 64: return run_gemm<64, BF16>(x, q, s, y, M, K, N, G, dev, st);
+    case 128: return run_gemm<128, BF16>(x, q, s, y, M, K, N, G, dev, st);
+    default: return run_gemm<256, BF16>(x, q, s, y, M, K, N, G, dev, st);
+  }
+}
+
+// Token-tile heuristic: the smallest BT that covers M, capped at 256; for
+// larger M pick between 128 and 256 by the number of tile waves.
+int pick_bt(int M, int N, int sm_count) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  const int nt = (N + kTileN - 1) / kTileN;
+  auto cost = [&](int bt) {
+    const long long tiles = static_cast<long long>(nt) * ((M + bt - 1) / bt);
+    const long long waves = (tiles + sm_count - 1) / sm_count;
+    return waves * (bt + 32);  // per-tile time ~ BT plus a fixed pipeline fill
+  };
+  return cost(128) < cost(256) ? 128 : 256;
+}
+
+}  // namespace
+}  // namespace ngb
+
+extern "C" int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight,
+                             const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                             int tile_tokens, void* stream) {
+  using namespace ngb;
+  if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || K <= 0 || N <= 0 || K % kBK != 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (static_cast<long long>(M) * N >= (1LL << 40) || K / 8 > (1 << 30)) return NG_ERR_BAD_SHAPE;
+  if (tile_tokens != 0 && tile_tokens != 16 && tile_tokens != 32 && tile_tokens != 64 &&
+      tile_tokens != 128 && tile_tokens != 256)
+    return NG_ERR_BAD_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 2) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  const int bt = tile_tokens ? tile_tokens : pick_bt(M, N, dev.sm_count);
+  auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NG_DTYPE_BF16)
+    return dispatch_bt<true>(bt, x, qweight, s, y, M, K, N, group_size, dev, strm);
+  return dispatch_bt<false>(bt, x, qweight, s, y, M, K, N, group_size, dev, strm);
 }
