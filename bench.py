@@ -1,0 +1,335 @@
+"""Benchmark of the W4A16 hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gemv|gemm]
+
+Workload (default ``gemv``): BASELINE config 1 -- the decode GEMV
+Y[1, 14336] = X[1, 4096] @ W4(4096 x 14336), group 128, fp16 activations, the
+shape the headline "decode GEMV us & HBM GB/s at M=1" is quoted on.  A step is
+one fused dequant-GEMV over one batch.  ``--workload gemm`` times BASELINE
+config 3's M=2048, K=4096, N=14336 prefill GEMM instead (TFLOP/s).
+
+* ``value``: algorithmic bytes (``K*N/2 + K/G*N*2 + M*K*2 + M*N*2``, the
+  reference's byte model, bench/harness.py:243-255) per step x steps x ranks,
+  divided by the device time of the timed region (CUDA events on the launching
+  stream, max over ranks).  Inputs are resident in HBM; the weight rotates
+  over enough distinct copies to exceed L2 (so every step reads HBM).  The
+  K steps are replayed from one CUDA graph so launch gaps are the device's.
+* ``e2e``: the same metric through the public API (``nibblegemm_b200.gemv``)
+  with the activation copied host->device from pinned memory and the result
+  copied back every step, host-synchronised -- what a caller sees.
+* ``roofline``: the GEMV kernel's achieved HBM GB/s against the measured copy
+  bandwidth in MEASURED_PEAKS.json (burst figure: the kernel is timed alone).
+* ``cpu_baseline``: the reference's CPU path (numpy unpack + fp32 dequantise +
+  fp32 matmul, restated in ``oracle/quant_oracle.py``) on a bounded sample.
+* ``--impl reference``: that CPU path alone, all host threads, as the
+  reference arm (rank 0 only under torchrun).
+
+Multi-GPU: the GEMV does not shard -- ranks run independent replicas (weak
+scaling, no collective on the data path).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode GEMV µs & HBM GB/s (% of 8 TB/s) at M=1; prefill TFLOP/s; 8B tok/s @1/2/4/8"
+WORKLOADS = {
+    "gemv": dict(M=1, K=4096, N=14336, G=128, name="W4A16 decode GEMV M=1 K=4096 N=14336 g128 fp16 (BASELINE config 1)"),
+    "gemm": dict(M=2048, K=4096, N=14336, G=128, name="W4A16 prefill GEMM M=2048 K=4096 N=14336 g128 fp16 (BASELINE config 3)"),
+}
+
+
+def algo_bytes(M, K, N, G):
+    return K * N // 2 + (K // G) * N * 2 + M * K * 2 + M * N * 2
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [int(r[0]) for r in self.rows if r[0].isdigit()]
+        mx = [int(r[1]) for r in self.rows if r[1].isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 2 + i and r[2 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_reference_sample(wl, seconds: float = 12.0, threads: int = 0):
+    """Time the reference's CPU path (oracle port) on config shapes; returns
+    (GB/s in the same byte model, sample description, threads used)."""
+    from oracle import quant_oracle as qo
+    M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
+    if threads > 0:
+        torch.set_num_threads(threads)
+    x, q, s = qo.synthetic_case(M, K, N, group_size=G, seed=1)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        W = qo.dequantize_np(q, s, G, K).astype(np.float32)
+        _ = (torch.from_numpy(x.astype(np.float32)) @ torch.from_numpy(W)).to(torch.float16)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or calls >= 50:
+            break
+    per = el / calls
+    return (algo_bytes(M, K, N, G) / per / 1e9, per,
+            f"{calls} full reference_matmul calls (numpy dequantise + torch fp32 matmul) at M={M} K={K} N={N}",
+            torch.get_num_threads())
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    wl = WORKLOADS[args.workload]
+    M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
+    from oracle import quant_oracle as qo
+    x, q, s = qo.synthetic_case(M, K, N, group_size=G, seed=1)
+    xt = torch.from_numpy(x.astype(np.float32))
+
+    def step():
+        W = qo.dequantize_np(q, s, G, K).astype(np.float32)
+        return (xt @ torch.from_numpy(W)).to(torch.float16)
+
+    # Each step is one full reference call (seconds on a CPU): warm-up and the
+    # timed steps are capped so the arm ends within a few minutes; the line
+    # reports the steps actually timed.
+    for _ in range(min(args.warmup, 3)):
+        step()
+    t0, done = time.perf_counter(), 0
+    while done < args.steps:
+        step()
+        done += 1
+        if time.perf_counter() - t0 > 90.0:
+            break
+    el = time.perf_counter() - t0
+    per = el / done
+    args.steps, args.warmup = done, min(args.warmup, 3)
+    if args.workload == "gemv":
+        value, unit = algo_bytes(M, K, N, G) / per / 1e9, "GB/s"
+    else:
+        value, unit = 2.0 * M * K * N / per / 1e12, "TFLOP/s"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (BASELINE distributions, seeded)",
+        "config": {"workload": wl["name"], "M": M, "K": K, "N": N, "group_size": G,
+                   "l2": "n/a (host)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{args.steps} timed reference_matmul calls (numpy unpack + fp32 dequantise + torch fp32 matmul)"},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="gemv")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import nibblegemm_b200 as ng
+    from nibblegemm_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    wl = WORKLOADS[args.workload]
+    M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
+    from oracle import quant_oracle as qo  # seeded synthetic inputs (generator only)
+    x, q, s = qo.synthetic_case(M, K, N, group_size=G, seed=1 + rank)
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    wbytes = q.nbytes + s.nbytes
+    nrot = max(2, -(-3 * l2 // wbytes))
+    qw_dev = [ng.QuantizedWeight(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), G, K, N)
+              for _ in range(nrot)]
+    X = torch.from_numpy(x).cuda()
+    Y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ext = ng.extension()
+    if args.workload == "gemv":
+        op = lambda i: ext.gemv_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G, out=Y)
+    else:
+        op = lambda i: ext.gemm_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G, out=Y)
+
+    # ---- device-timed region: K steps replayed from one CUDA graph ----------------
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            op(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            op(i)
+    graph.replay()  # warm the graph itself
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    assert ext.device_status() == 0, "a kernel reported a bounded-wait timeout"
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    per_ms = ms / args.steps
+    nbytes = algo_bytes(M, K, N, G)
+    flops = 2.0 * M * K * N
+    if args.workload == "gemv":
+        value, unit = nbytes * args.steps * world / (ms * 1e-3) / 1e9, "GB/s"
+    else:
+        value, unit = flops * args.steps * world / (ms * 1e-3) / 1e12, "TFLOP/s"
+
+    # ---- end-to-end through the public API with host buffers ----------------------
+    x_host = torch.from_numpy(x).pin_memory()
+    y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    e2e_steps = max(20, min(args.steps, 200))
+    fn = ng.gemv if args.workload == "gemv" else ng.gemm
+    for i in range(3):
+        y_host.copy_(fn(x_host.cuda(non_blocking=True), qw_dev[i % nrot]), non_blocking=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        xd = x_host.cuda(non_blocking=True)
+        y_host.copy_(fn(xd, qw_dev[i % nrot]), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    if args.workload == "gemv":
+        e2e_val = nbytes * e2e_steps * world / (e2e_ms * 1e-3) / 1e9
+    else:
+        e2e_val = flops * e2e_steps * world / (e2e_ms * 1e-3) / 1e12
+
+    if rank == 0:
+        hbm, tf, src = measured_peaks()
+        if args.workload == "gemv":
+            achieved = nbytes / (per_ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(achieved / hbm, 4), "traffic": None,
+                    "peak_source": f"{src} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                    "algorithmic_bytes_per_launch": nbytes}
+        else:
+            achieved = flops / (per_ms * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf, "unit": "TFLOP/s",
+                    "frac": round(achieved / tf, 4), "traffic": None,
+                    "peak_source": f"{src} cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops)",
+                    "algorithmic_flops_per_launch": flops}
+        traffic_file = os.path.join(ROOT, "profiles", f"traffic_{args.workload}.json")
+        if os.path.exists(traffic_file):
+            roof["traffic"] = json.load(open(traffic_file)).get("dram_bytes_per_launch")
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (BASELINE distributions: codes U[0,15], scales |N(0,1)|*0.02+1e-3, X~N(0,1); seeded)",
+            "config": {"workload": wl["name"], "M": M, "K": K, "N": N, "group_size": G,
+                       "l2": f"weights rotated over {nrot} copies ({nrot * wbytes / 1e6:.0f} MB > L2 {l2 / 1e6:.0f} MB)",
+                       "parallelism": f"replicas x{world}", "timing": "one CUDA graph of `steps` launches"},
+            "roofline": roof,
+            "e2e": {"value": round(e2e_val, 2), "unit": unit, "h2d_bytes_per_step": M * K * 2,
+                    "d2h_bytes_per_step": M * N * 2, "steps": e2e_steps,
+                    "path": "nibblegemm_b200.gemv/gemm with pinned host X in, Y out, host sync per step"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "us_per_step": round(per_ms * 1e3, 3),
+        }
+        if not args.no_cpu_baseline:
+            v, per, sample, cores = cpu_reference_sample(wl)
+            if args.workload == "gemm":
+                v = flops / per / 1e12
+            line["cpu_baseline"] = {"value": round(v, 6), "unit": unit,
+                                    "cores": cores, "kind": "port", "sample": sample,
+                                    "ms_per_call": round(per * 1e3, 1)}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
