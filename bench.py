@@ -237,6 +237,13 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        # Keep the GPU busy with the same graph for ~0.5 s first so the
+        # sampler (100 ms period) sees clocks under this load; the timed
+        # region below is one replay of exactly `steps` launches.
+        t_end = time.perf_counter() + 0.5
+        while time.perf_counter() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             start.record(stream)
             graph.replay()

@@ -1,5 +1,7 @@
 // Library-wide C-ABI pieces: status strings, version, per-device property
 // cache and the per-device error word that bounded waits report through.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "ng_common.cuh"
@@ -47,6 +49,20 @@ int current_device_info(DeviceInfo* out) {
   if (g_status[dev] != NG_OK) return g_status[dev];
   *out = g_info[dev];
   return NG_OK;
+}
+
+void* tensor_map_encode_fn() {
+  static void* fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = p;
+  });
+  return fn;
 }
 
 }  // namespace ngb

@@ -192,58 +192,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ dequant
     const int t = threadIdx.x - 256;  // weight column within the tile
     const int atom = t >> 3, r8 = t & 7;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+    const int my_tiles = tiles > static_cast<int>(blockIdx.x)
+                             ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                             : 0;
+    const int total = my_tiles * kb_count;
+    // Scale of iteration i (flattened over this CTA's tiles x k-steps); loaded
+    // kPrefetch iterations ahead so its global-memory latency never sits
+    // between a stage landing and its decode.
+    auto scale_at = [&](int i) -> __half {
+      if (i >= total) return __float2half(0.f);
+      const int tile = static_cast<int>(blockIdx.x) + (i / kb_count) * static_cast<int>(gridDim.x);
       const int n = (tile % n_tiles) * kTileN + t;
-      const bool n_ok = n < N;
-      bool ok = true;
-      for (int kb = 0; kb < kb_count; ++kb, ++it) {
-        const int s = it % stages;
-        const uint32_t ph = (it / stages) & 1;
-        const int g = (kb * kBK) / G;
-        const __half sc = n_ok ? scales[static_cast<size_t>(g) * N + n] : __float2half(0.f);
-        if (!mbar_wait_bounded(&bars->full[s], ph, err, abort)) {
-          ok = false;
-          break;
-        }
-        unsigned char* st = smem + s * kStageBytes;
-        const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + kBTileBytes);
-        unsigned char* arow = st + atom * 1024 + r8 * 128;
+      const int g = ((i % kb_count) * kBK) / G;
+      return n < N ? scales[static_cast<size_t>(g) * N + n] : __float2half(0.f);
+    };
+    constexpr int kPrefetch = 4;
+    __half pf[kPrefetch];
 #pragma unroll
-        for (int r = 0; r < kBK / 8; ++r) {
-          const uint32_t q = raw[r * kTileN + t];
-          uint4 v;
-          if constexpr (!BF16) {
-            __half2 w[4];
-            decode8_f16(q, w);
-            const __half2 s2 = __half2half2(sc);
-            v.x = h2_bits(__hmul2(w[0], s2));
-            v.y = h2_bits(__hmul2(w[1], s2));
-            v.z = h2_bits(__hmul2(w[2], s2));
-            v.w = h2_bits(__hmul2(w[3], s2));
-          } else {
-            const uint32_t q16 = q >> 16;
-            const float sf = __half2float(sc);
-            const f2 s2 = f2_make(sf, sf);
-            const f2 p[4] = {decode_pair_f32<0>(q, q16), decode_pair_f32<1>(q, q16),
-                             decode_pair_f32<2>(q, q16), decode_pair_f32<3>(q, q16)};
-            uint32_t b[4];
+    for (int j = 0; j < kPrefetch; ++j) pf[j] = scale_at(j);
+    for (int it = 0; it < total; ++it) {
+      const int s = it % stages;
+      const uint32_t ph = (it / stages) & 1;
+      const __half sc = pf[0];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float lo, hi;
-              f2_split(f2_mul(p[j], s2), lo, hi);
-              const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
-              b[j] = *reinterpret_cast<const uint32_t*>(&bb);
-            }
-            v = make_uint4(b[0], b[1], b[2], b[3]);
+      for (int j = 0; j + 1 < kPrefetch; ++j) pf[j] = pf[j + 1];
+      pf[kPrefetch - 1] = scale_at(it + kPrefetch);
+      if (!mbar_wait_bounded(&bars->full[s], ph, err, abort)) break;
+      unsigned char* st = smem + s * kStageBytes;
+      const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + kBTileBytes);
+      unsigned char* arow = st + atom * 1024 + r8 * 128;
+      uint32_t qv[kBK / 8];
+#pragma unroll
+      for (int r = 0; r < kBK / 8; ++r) qv[r] = raw[r * kTileN + t];
+#pragma unroll
+      for (int r = 0; r < kBK / 8; ++r) {
+        const uint32_t q = qv[r];
+        uint4 v;
+        if constexpr (!BF16) {
+          __half2 w[4];
+          decode8_f16(q, w);
+          const __half2 s2 = __half2half2(sc);
+          v.x = h2_bits(__hmul2(w[0], s2));
+          v.y = h2_bits(__hmul2(w[1], s2));
+          v.z = h2_bits(__hmul2(w[2], s2));
+          v.w = h2_bits(__hmul2(w[3], s2));
+        } else {
+          const uint32_t q16 = q >> 16;
+          const float sf = __half2float(sc);
+          const f2 s2 = f2_make(sf, sf);
+          const f2 p[4] = {decode_pair_f32<0>(q, q16), decode_pair_f32<1>(q, q16),
+                           decode_pair_f32<2>(q, q16), decode_pair_f32<3>(q, q16)};
+          uint32_t bw[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float lo, hi;
+            f2_split(f2_mul(p[j], s2), lo, hi);
+            const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
+            bw[j] = *reinterpret_cast<const uint32_t*>(&bb);
           }
-          *reinterpret_cast<uint4*>(arow + ((r ^ r8) << 4)) = v;
+          v = make_uint4(bw[0], bw[1], bw[2], bw[3]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->afull[s]);
+        *reinterpret_cast<uint4*>(arow + ((r ^ r8) << 4)) = v;
       }
-      if (!ok) break;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->afull[s]);
     }
   }
 
@@ -266,23 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
-                                         &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 int make_maps(const void* x, const int32_t* q, int M, int K, int N, int BT, CUtensorMap* mx,
               CUtensorMap* mq) {
-  auto enc = encode_fn();
+  auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encode_fn());
   if (!enc) return NG_ERR_CUDA;
   {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};

@@ -344,29 +344,10 @@ int dispatch_w(int threads, const void* x, const uint32_t* qw, const __half* s, 
 }
 
 }  // namespace
-}  // namespace ngb
-
-extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
-                             const uint16_t* scales, void* y, int M, int K, int N, int group_size,
-                             int splits, int block_threads, int algo, void* stream) {
-  using namespace ngb;
-  if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
-  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
-  if (M < 1 || M > 16 || K <= 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
-  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
-  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
-  if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
-  if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
-  if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
-  if (algo < 0 || algo > 2) return NG_ERR_BAD_ARGUMENT;
-  if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
-  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
-    return NG_ERR_MISALIGNED;
-  DeviceInfo dev;
-  if (int st = current_device_info(&dev)) return st;
-  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
-  const auto* s = reinterpret_cast<const __half*>(scales);
-  auto strm = static_cast<cudaStream_t>(stream);
+// Cluster split-K launcher (no workspace); validated by the caller.
+int gemv_cluster(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M,
+                 int K, int N, int group_size, int splits, int block_threads, int algo,
+                 const DeviceInfo& dev, cudaStream_t strm) {
   const int threads = block_threads ? block_threads : 256;
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_w<true, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
@@ -374,3 +355,5 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
     return dispatch_w<false, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
   return dispatch_w<false, kHalf2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
 }
+
+}  // namespace ngb

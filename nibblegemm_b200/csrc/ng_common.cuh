@@ -122,6 +122,16 @@ struct DeviceInfo {
 // Cached properties of the current device; returns NG_OK or an error status.
 int current_device_info(DeviceInfo* out);
 
+// The driver's cuTensorMapEncodeTiled (fetched once through the runtime's
+// driver entry-point query, so the library needs no libcuda link), as an
+// opaque pointer; nullptr if unavailable.
+void* tensor_map_encode_fn();
+
+// Cluster split-K GEMV launcher (gemv.cu); arguments already validated.
+int gemv_cluster(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M,
+                 int K, int N, int group_size, int splits, int block_threads, int algo,
+                 const DeviceInfo& dev, cudaStream_t strm);
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }
