@@ -86,8 +86,10 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     column tiles split between CTAs are finished by the last CTA to arrive,
  *     which sums the partials in CTA order (deterministic).
  *     `workspace` must hold ng_gemv_workspace_bytes(M, N) bytes, be 256-byte
- *     aligned and be zero-filled before its first use; every call leaves it
- *     zero-filled again.  Calls that share a workspace must not overlap on
+ *     aligned and be zero-filled before its first use.  Its layout does not
+ *     depend on M or N, and every call leaves the part that must start at zero
+ *     (per-tile arrival counters) zero again, so one workspace serves any
+ *     sequence of shapes.  Calls that share a workspace must not overlap on
  *     the GPU (use one workspace per stream).
  *   - cluster split-K (workspace == NULL, or splits / block_threads given):
  *     `splits` K slices (1..16, 0 = heuristic) reduced through distributed

@@ -11,15 +11,15 @@
 //   * small batches (M = 16 .. 128) use a narrow N side instead of padding a
 //     128-row M side.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over tiles):
+// Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: packed weight tile [8 words x 128 columns] and
 //               the X tile [BT rows x 64 values, 128-byte swizzle] per k-step
 //   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16 each) per k-step, commit
 //               to the stage's "empty" barrier; per tile, commit to "acc full"
 //   warp 2      tensor-memory allocator (2 x BT columns: double-buffered acc)
 //   warps 4-7   epilogue: tcgen05.ld 128 lanes x BT columns -> fp16/bf16 -> Y
-//   warps 8-11  dequant: thread t owns weight column n0 + t; per k-step it
-//               decodes 8 packed words (64 values of K) with the magic-number
+//   warps 8-15  dequant: two threads per weight column (n0 + t), each takes 4
+//               of the 8 packed rows of a k-step; it decodes them with the magic-number
 //               method, applies the group scale (one rounding, so the fp16
 //               operand equals the reference's dequantised weight bit for
 //               bit), and writes one 128-byte row of the A tile in the
@@ -40,7 +40,8 @@ namespace {
 
 constexpr int kTileN = 128;        // weight columns per tile (MMA M)
 constexpr int kBK = 64;            // values of K per k-step (one 128-byte swizzle row)
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
+constexpr int kDequantWarps = 8;  // warps 8..15: two threads per weight column
 constexpr int kATileBytes = kTileN * kBK * 2;   // 16 KB decoded weights
 constexpr int kRawBytes = (kBK / 8) * kTileN * 4;  // 4 KB packed words
 constexpr int kSmemBudget = 220 * 1024;
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->afull[s], 4);
+      mbar_init(&bars->afull[s], kDequantWarps);
       mbar_init(&bars->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -190,7 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
-    const int t = threadIdx.x - 256;  // weight column within the tile
+    const int t = (threadIdx.x - 256) & (kTileN - 1);  // weight column within the tile
+    const int half = (threadIdx.x - 256) >> 7;           // which 4 of the 8 packed rows
     const int atom = t >> 3, r8 = t & 7;
     const int my_tiles = tiles > static_cast<int>(blockIdx.x)
                              ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
@@ -221,12 +223,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       unsigned char* st = smem + s * kStageBytes;
       const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + kBTileBytes);
       unsigned char* arow = st + atom * 1024 + r8 * 128;
-      uint32_t qv[kBK / 8];
+      constexpr int kRowsPer = kBK / 16;  // 4 packed rows per thread
+      uint32_t qv[kRowsPer];
 #pragma unroll
-      for (int r = 0; r < kBK / 8; ++r) qv[r] = raw[r * kTileN + t];
+      for (int i = 0; i < kRowsPer; ++i) qv[i] = raw[(half * kRowsPer + i) * kTileN + t];
 #pragma unroll
-      for (int r = 0; r < kBK / 8; ++r) {
-        const uint32_t q = qv[r];
+      for (int i = 0; i < kRowsPer; ++i) {
+        const int r = half * kRowsPer + i;
+        const uint32_t q = qv[i];
         uint4 v;
         if constexpr (!BF16) {
           __half2 w[4];

@@ -317,13 +317,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-size_t ws_partial_offset(int N) {
-  const size_t cnt = static_cast<size_t>((N + kCols - 1) / kCols) * 4;
-  return (cnt + 255) / 256 * 256;
-}
+// Workspace layout, fixed for a device whatever M and N are (so calls with
+// different shapes can share one workspace): partial-sum slots for the
+// largest M tile first (2 per CTA), then one arrival counter per column tile.
+// Only the counters must be zero between calls; the kernel re-zeroes them.
+size_t ws_counter_offset(int P) { return static_cast<size_t>(2) * P * 16 * kCols * 4; }
 
-size_t ws_bytes(int MT, int N, int P) {
-  return ws_partial_offset(N) + static_cast<size_t>(2) * P * MT * kCols * 4;
+size_t ws_bytes(int /*MT*/, int N, int P) {
+  return ws_counter_offset(P) + static_cast<size_t>((N + kCols - 1) / kCols) * 4;
 }
 
 int mt_of(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
@@ -366,8 +367,9 @@ int run_sk(const void* x, const uint32_t* q, const __half* s, void* y, int M, in
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 8192);
   });
-  auto* counters = static_cast<unsigned int*>(ws);
-  auto* partials = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + ws_partial_offset(N));
+  auto* partials = static_cast<float*>(ws);
+  auto* counters = reinterpret_cast<unsigned int*>(static_cast<unsigned char*>(ws) +
+                                                   ws_counter_offset(dev.sm_count));
   kern<<<P, kThreads, smem, stream>>>(mw, mx, s, y, M, K, N, G, units, chunks, stages, counters,
                                       partials, dev.err);
   return launch_status();
