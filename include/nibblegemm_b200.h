@@ -74,43 +74,29 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
                   int K, int N, int group_size, int fast, void* stream);
 
 /*
- * Decode-regime fused dequant GEMV, one launch.
+ * Decode-regime fused dequant GEMV, one launch, no workspace.
  * Replaces the reference's `gemv_w4a16(X, Wq, S, group_size, version,
  * splits_override, threads_override)` (csrc/gemv_w4a16.cu:341-425, bound at
- * csrc/bindings.cpp:12-15); that function allocates its split-K workspace
- * from the caching allocator per call, this one takes it from the caller.
+ * csrc/bindings.cpp:12-15).  The reference reduces its K splits through an
+ * fp32 workspace and a second kernel; here the CTAs of one column tile form a
+ * thread-block cluster and reduce through distributed shared memory, in fixed
+ * rank order (deterministic).
  *   M in [1, 16]; N % 4 == 0; group_size in {64, 128, 256}; K % group_size == 0.
- *   Two schedules:
- *   - stream-K (default: workspace != NULL, splits == 0, block_threads == 0):
- *     one CTA per SM, equal byte share per SM, TMA-fed shared-memory rings;
- *     column tiles split between CTAs are finished by the last CTA to arrive,
- *     which sums the partials in CTA order (deterministic).
- *     `workspace` must hold ng_gemv_workspace_bytes(M, N) bytes, be 256-byte
- *     aligned and be zero-filled before its first use.  Its layout does not
- *     depend on M or N, and every call leaves the part that must start at zero
- *     (per-tile arrival counters) zero again, so one workspace serves any
- *     sequence of shapes.  Calls that share a workspace must not overlap on
- *     the GPU (use one workspace per stream).
- *   - cluster split-K (workspace == NULL, or splits / block_threads given):
- *     `splits` K slices (1..16, 0 = heuristic) reduced through distributed
- *     shared memory within a thread-block cluster; no workspace.
- *     block_threads: 0 = heuristic (256), else 128 or 256.
+ *   splits: number of K slices (cluster size), 0 = heuristic, else 1..16; it
+ *           is raised when needed so each slice's activations fit on chip.
+ *   block_threads: 0 = heuristic (256), else 128 or 256.
  *   algo: 0 = default for the dtype; 1 = fp16 magic decode with packed-half2
  *         FMA windows of 32 values flushed to fp32 (fp16 x only);
  *         2 = fp32 magic decode with packed fp32x2 FMA, fp32 throughout.
  *         Default: 1 for fp16 x, 2 for bf16 x.
+ *   Launched with programmatic stream serialisation: it starts streaming its
+ *   (read-only) weights while the previous kernel on the stream finishes and
+ *   reads x / writes y only after that kernel has completed.
  *   x, qweight 16-byte aligned; scales 8-byte aligned.
  */
 int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
                   void* y, int M, int K, int N, int group_size, int splits, int block_threads,
-                  int algo, void* workspace, size_t workspace_bytes, void* stream);
-
-/*
- * Workspace bytes the stream-K GEMV needs for M rows and N columns on the
- * current device (0 if M or N is out of range).  No counterpart in the
- * reference (which allocates its workspace internally per call).
- */
-size_t ng_gemv_workspace_bytes(int M, int N);
+                  int algo, void* stream);
 
 /*
  * Prefill-regime fused dequant GEMM on the sm_100 tensor cores: tcgen05.mma

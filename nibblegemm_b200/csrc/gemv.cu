@@ -16,6 +16,16 @@
 //     that is 64-128 KB per SM, comfortably above the bandwidth-latency product.
 //   * Activations for the CTA's K slice are staged once in shared memory (in
 //     the accumulation type) and read as broadcasts.
+//   * Each warp software-pipelines its chunks: the next chunk's eight loads
+//     are issued before the current chunk is decoded.
+//   * Programmatic dependent launch: the kernel is launched with programmatic
+//     stream serialisation, signals `griddepcontrol.launch_dependents` on
+//     entry and issues its first weight loads *before* `griddepcontrol.wait`.
+//     Weights are read-only, so a GEMV streams its weights while the kernel
+//     before it on the stream drains; activations are read and Y written only
+//     after the wait, so the data dependency on the previous kernel holds.
+//     Back-to-back decode GEMVs (a model's layer sequence) thereby hide the
+//     launch and ramp-up latency that dominates a ~5 us kernel.
 //
 // Two accumulation paths:
 //   * kHalf2 (fp16 activations): the fp16 magic-number decode, packed half2
@@ -42,7 +52,14 @@ constexpr int kCols = 128;  // columns per CTA tile
 constexpr int kU = 8;       // packed rows per chunk
 constexpr int kWin = 4;     // half2 path: packed rows per fp16 accumulation window
 constexpr int kMaxCluster = 16;
-constexpr int kStageBytes = 32 * 1024;  // activation staging budget per slab
+constexpr int kStageBudget = 160 * 1024;  // activation staging limit (bytes)
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 
 enum Path { kHalf2 = 0, kFloat2 = 1 };
 
@@ -50,11 +67,11 @@ template <int MT, bool XBF16, int PATH, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
     gemv_kernel(const void* __restrict__ x, const uint32_t* __restrict__ qw,
                 const __half* __restrict__ scales, void* __restrict__ y, int M, int K, int N,
-                int G, int rows_per_cta, int slab_rows, int csize) {
+                int G, int rows_per_cta, int csize) {
   extern __shared__ __align__(16) unsigned char smem[];
   using XS = typename std::conditional<PATH == kFloat2, float, __half>::type;
   XS* xs = reinterpret_cast<XS*>(smem);
-  const int xstride = slab_rows * 8;  // staged elements per row of X
+  const int xstride = rows_per_cta * 8;  // staged elements per row of X
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -73,147 +90,163 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[c][m] = 0.f;
 
-  for (int s0 = kr0; s0 < kr1; s0 += slab_rows) {
-    const int nrows = min(slab_rows, kr1 - s0);
-    __syncthreads();  // previous slab fully consumed
-    // ---- stage X[:, s0*8 : (s0+nrows)*8) -------------------------------------
-    for (int i = tid; i < MT * nrows; i += WARPS * 32) {
-      const int m = i / nrows;
-      const int r = i - m * nrows;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (m < M) v = ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(s0 + r) * 8);
-      XS* dst = xs + m * xstride + r * 8;
-      if constexpr (PATH == kFloat2) {
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        float f[8];
+  griddep_launch_dependents();
+  const int nrows = max(0, kr1 - kr0);
+  const int nch = nrows / kU;
+  auto load_chunk = [&](int ch, uint4 (&q)[kU], uint2& sv) {
+    const int r0 = kr0 + ch * kU;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if constexpr (XBF16) {
-            f[2 * j] = __uint_as_float(w[j] << 16);
-            f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
-          } else {
-            const float2 t = __half22float2(h2_from_bits(w[j]));
-            f[2 * j] = t.x;
-            f[2 * j + 1] = t.y;
-          }
-        }
-        reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
-        reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
-      } else {
-        *reinterpret_cast<uint4*>(dst) = v;
-      }
-    }
-    __syncthreads();
+    for (int u = 0; u < kU; ++u)
+      q[u] = col_ok ? ld_stream_v4(qw + static_cast<size_t>(r0 + u) * N + col, pol)
+                    : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+    const int grp = (r0 * 8) / G;
+    sv = col_ok ? ld_ro_v2(scales + static_cast<size_t>(grp) * N + col) : make_uint2(0u, 0u);
+  };
+  auto process = [&](int ch, const uint4 (&q)[kU], uint2 sv) {
+    const int r0 = kr0 + ch * kU;
+    float sc[4];
+    sc[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFF)));
+    sc[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
+    sc[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFF)));
+    sc[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
+    const XS* xc = xs + (r0 - kr0) * 8;
 
-    // ---- stream the weights ---------------------------------------------------
-    const int nch = nrows / kU;
-    for (int ch = warp; ch < nch; ch += WARPS) {
-      const int r0 = s0 + ch * kU;
-      uint4 q[kU];
+    if constexpr (PATH == kHalf2) {
 #pragma unroll
-      for (int u = 0; u < kU; ++u)
-        q[u] = col_ok ? ld_stream_v4(qw + static_cast<size_t>(r0 + u) * N + col, pol)
-                      : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-      const int grp = (r0 * 8) / G;
-      const uint2 sv = col_ok ? ld_ro_v2(scales + static_cast<size_t>(grp) * N + col)
-                              : make_uint2(0u, 0u);
-      float sc[4];
-      sc[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFF)));
-      sc[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
-      sc[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFF)));
-      sc[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
-      const XS* xc = xs + (r0 - s0) * 8;
-
-      if constexpr (PATH == kHalf2) {
-#pragma unroll
-        for (int win = 0; win < kU / kWin; ++win) {
-          __half2 h[4][MT];
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) h[c][m] = __float2half2_rn(0.f);
-#pragma unroll
-          for (int rr = 0; rr < kWin; ++rr) {
-            const int u = win * kWin + rr;
-            const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-            __half2 wv[4][4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) decode8_f16(words[c], wv[c]);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              const uint4 xv = *reinterpret_cast<const uint4*>(xc + m * xstride + u * 8);
-              const __half2 xh[4] = {h2_from_bits(xv.x), h2_from_bits(xv.y), h2_from_bits(xv.z),
-                                     h2_from_bits(xv.w)};
-#pragma unroll
-              for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) h[c][m] = __hfma2(wv[c][i], xh[i], h[c][m]);
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              const float2 f = __half22float2(h[c][m]);
-              acc[c][m] = fmaf(f.x + f.y, sc[c], acc[c][m]);
-            }
-        }
-      } else {
-        constexpr bool kScaleEarly = MT >= 8;
-        f2 a2[4][MT];
+      for (int win = 0; win < kU / kWin; ++win) {
+        __half2 h[4][MT];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int m = 0; m < MT; ++m) a2[c][m] = f2_make(0.f, 0.f);
-        f2 s2[4];
+          for (int m = 0; m < MT; ++m) h[c][m] = __float2half2_rn(0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) s2[c] = f2_make(sc[c], sc[c]);
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
+        for (int rr = 0; rr < kWin; ++rr) {
+          const int u = win * kWin + rr;
           const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-          f2 wv[4][4];
+          __half2 wv[4][4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t w16 = words[c] >> 16;
-            wv[c][0] = decode_pair_f32<0>(words[c], w16);
-            wv[c][1] = decode_pair_f32<1>(words[c], w16);
-            wv[c][2] = decode_pair_f32<2>(words[c], w16);
-            wv[c][3] = decode_pair_f32<3>(words[c], w16);
-            if constexpr (kScaleEarly) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) wv[c][j] = f2_mul(wv[c][j], s2[c]);
-            }
-          }
+          for (int c = 0; c < 4; ++c) decode8_f16(words[c], wv[c]);
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
-            const float4 xa = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8);
-            const float4 xb = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8 + 4);
-            const f2 xp[4] = {f2_make(xa.x, xa.y), f2_make(xa.z, xa.w), f2_make(xb.x, xb.y),
-                              f2_make(xb.z, xb.w)};
+            const uint4 xv = *reinterpret_cast<const uint4*>(xc + m * xstride + u * 8);
+            const __half2 xh[4] = {h2_from_bits(xv.x), h2_from_bits(xv.y), h2_from_bits(xv.z),
+                                   h2_from_bits(xv.w)};
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
-              for (int j = 0; j < 4; ++j) a2[c][m] = f2_fma(wv[c][j], xp[j], a2[c][m]);
+              for (int i = 0; i < 4; ++i) h[c][m] = __hfma2(wv[c][i], xh[i], h[c][m]);
           }
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
-            float lo, hi;
-            f2_split(a2[c][m], lo, hi);
-            if constexpr (kScaleEarly)
-              acc[c][m] += lo + hi;
-            else
-              acc[c][m] = fmaf(lo + hi, sc[c], acc[c][m]);
+            const float2 f = __half22float2(h[c][m]);
+            acc[c][m] = fmaf(f.x + f.y, sc[c], acc[c][m]);
           }
       }
+    } else {
+      constexpr bool kScaleEarly = MT >= 8;
+      f2 a2[4][MT];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) a2[c][m] = f2_make(0.f, 0.f);
+      f2 s2[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s2[c] = f2_make(sc[c], sc[c]);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+        f2 wv[4][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t w16 = words[c] >> 16;
+          wv[c][0] = decode_pair_f32<0>(words[c], w16);
+          wv[c][1] = decode_pair_f32<1>(words[c], w16);
+          wv[c][2] = decode_pair_f32<2>(words[c], w16);
+          wv[c][3] = decode_pair_f32<3>(words[c], w16);
+          if constexpr (kScaleEarly) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) wv[c][j] = f2_mul(wv[c][j], s2[c]);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const float4 xa = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8);
+          const float4 xb = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8 + 4);
+          const f2 xp[4] = {f2_make(xa.x, xa.y), f2_make(xa.z, xa.w), f2_make(xb.x, xb.y),
+                            f2_make(xb.z, xb.w)};
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a2[c][m] = f2_fma(wv[c][j], xp[j], a2[c][m]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float lo, hi;
+          f2_split(a2[c][m], lo, hi);
+          if constexpr (kScaleEarly)
+            acc[c][m] += lo + hi;
+          else
+            acc[c][m] = fmaf(lo + hi, sc[c], acc[c][m]);
+        }
     }
+
+  };
+
+  uint4 qa[kU], qb[kU];
+  uint2 sa = make_uint2(0u, 0u), sb = make_uint2(0u, 0u);
+  int ch = warp;
+  if (ch < nch) load_chunk(ch, qa, sa);  // weights only: no dependency on the previous kernel
+  griddep_wait();                          // activations / outputs of the previous kernel
+  // ---- stage X[:, kr0*8 : kr1*8) ------------------------------------------------
+  for (int i = tid; i < MT * nrows; i += WARPS * 32) {
+    const int m = i / nrows;
+    const int r = i - m * nrows;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (m < M) v = ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(kr0 + r) * 8);
+    XS* dst = xs + m * xstride + r * 8;
+    if constexpr (PATH == kFloat2) {
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (XBF16) {
+          f[2 * j] = __uint_as_float(w[j] << 16);
+          f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        } else {
+          const float2 t = __half22float2(h2_from_bits(w[j]));
+          f[2 * j] = t.x;
+          f[2 * j + 1] = t.y;
+        }
+      }
+      reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+    } else {
+      *reinterpret_cast<uint4*>(dst) = v;
+    }
+  }
+  __syncthreads();
+  // ---- stream the weights, one chunk ahead ------------------------------------
+  while (ch < nch) {
+    int nx = ch + WARPS;
+    if (nx < nch) load_chunk(nx, qb, sb);
+    process(ch, qa, sa);
+    ch = nx;
+    if (ch >= nch) break;
+    nx = ch + WARPS;
+    if (nx < nch) load_chunk(nx, qa, sa);
+    process(ch, qb, sb);
+    ch = nx;
   }
 
   // ---- CTA reduction over warps (fixed order) ---------------------------------
   constexpr int E = MT * kCols;
-  const size_t stage_bytes = static_cast<size_t>(MT) * xstride * sizeof(XS);
+  const size_t stage_bytes = static_cast<size_t>(MT) * xstride * sizeof(XS);  // staged X
   const size_t red_bytes = static_cast<size_t>(WARPS) * E * sizeof(float);
   float* red = reinterpret_cast<float*>(smem);
   float* fin = reinterpret_cast<float*>(smem + (stage_bytes > red_bytes ? stage_bytes : red_bytes));
@@ -297,16 +330,17 @@ int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int 
     const int target = dev.sm_count * occ_cache[d];
     C = std::max(1, target / std::max(1, col_tiles));
   }
+  // The CTA's whole activation slice is staged on chip: raise the split count
+  // (a request, not a promise) until it fits the staging budget.
+  const int max_rows = kStageBudget / (MT * 8 * esz);
+  C = std::max(C, (krows + max_rows - 1) / max_rows);
   C = std::min(C, kMaxCluster);
   C = std::max(1, std::min(C, krows / kU));
   int rows_per_cta = (krows + C - 1) / C;
   rows_per_cta = (rows_per_cta + kU - 1) / kU * kU;
   C = (krows + rows_per_cta - 1) / rows_per_cta;  // trim empty slices
-
-  int slab_max = kStageBytes / (MT * 8 * esz);
-  slab_max = std::max(kU, slab_max / kU * kU);
-  const int slab_rows = std::min(rows_per_cta, slab_max);
-  const size_t stage = static_cast<size_t>(MT) * slab_rows * 8 * esz;
+  if (static_cast<long long>(rows_per_cta) * MT * 8 * esz > kStageBudget) return NG_ERR_BAD_SHAPE;
+  const size_t stage = static_cast<size_t>(MT) * rows_per_cta * 8 * esz;
   const size_t red = static_cast<size_t>(WARPS) * MT * kCols * 4;
   const size_t smem = std::max(stage, red) + static_cast<size_t>(MT) * kCols * 4;
 
@@ -315,15 +349,16 @@ int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int 
   cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = C;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return launch_status(
-      cudaLaunchKernelEx(&cfg, kern, x, qw, s, y, M, K, N, G, rows_per_cta, slab_rows, C));
+  cfg.numAttrs = 2;
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, x, qw, s, y, M, K, N, G, rows_per_cta, C));
 }
 
 template <bool XBF16, int PATH, int WARPS>
@@ -344,10 +379,29 @@ int dispatch_w(int threads, const void* x, const uint32_t* qw, const __half* s, 
 }
 
 }  // namespace
-// Cluster split-K launcher (no workspace); validated by the caller.
-int gemv_cluster(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M,
-                 int K, int N, int group_size, int splits, int block_threads, int algo,
-                 const DeviceInfo& dev, cudaStream_t strm) {
+}  // namespace ngb
+
+extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
+                             const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                             int splits, int block_threads, int algo, void* stream) {
+  using namespace ngb;
+  if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
+  if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
+  if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
+  if (algo < 0 || algo > 2) return NG_ERR_BAD_ARGUMENT;
+  if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
   const int threads = block_threads ? block_threads : 256;
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_w<true, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
@@ -355,5 +409,3 @@ int gemv_cluster(const void* x, int x_dtype, const uint32_t* q, const __half* s,
     return dispatch_w<false, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
   return dispatch_w<false, kHalf2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
 }
-
-}  // namespace ngb

@@ -127,10 +127,6 @@ int current_device_info(DeviceInfo* out);
 // opaque pointer; nullptr if unavailable.
 void* tensor_map_encode_fn();
 
-// Cluster split-K GEMV launcher (gemv.cu); arguments already validated.
-int gemv_cluster(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M,
-                 int K, int N, int group_size, int splits, int block_threads, int algo,
-                 const DeviceInfo& dev, cudaStream_t strm);
 
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

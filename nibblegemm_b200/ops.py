@@ -77,22 +77,6 @@ class _Extension:
 
     def __init__(self):
         self.lib = _lib.load()
-        self._ws = {}  # (device index, stream handle) -> zero-initialised workspace
-
-    def workspace(self, M: int, N: int, device: torch.device, stream: int) -> torch.Tensor:
-        """The stream-K GEMV workspace for (device, stream), grown on demand.
-
-        Allocated zero-filled once; the kernel leaves it zero-filled after
-        every call, so it is reused as is (and stays valid under graph capture
-        once allocated).  One per stream: calls sharing one must not overlap.
-        """
-        need = self.lib.ng_gemv_workspace_bytes(M, N)
-        key = (device.index, stream)
-        ws = self._ws.get(key)
-        if ws is None or ws.numel() < need:
-            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
-            self._ws[key] = ws
-        return ws
 
     def dequant_w4(self, Wq: torch.Tensor, S: torch.Tensor, group_size: int, fast: bool = True,
                    out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
@@ -121,14 +105,10 @@ class _Extension:
         splits = 1 if version == 3 else int(splits_override)
         y = _out(out, M, N, X)
         with _on_device(X.device):
-            stream = torch.cuda.current_stream().cuda_stream
-            ws_ptr, ws_bytes = None, 0
-            if splits == 0 and threads_override == 0:
-                ws = self.workspace(M, N, X.device, stream)
-                ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
             st = self.lib.ng_gemv_w4a16(X.data_ptr(), _DTYPE_CODE[X.dtype], Wq.data_ptr(),
                                         S.data_ptr(), y.data_ptr(), M, K, N, int(group_size), splits,
-                                        int(threads_override), int(algo), ws_ptr, ws_bytes, stream)
+                                        int(threads_override), int(algo),
+                                        torch.cuda.current_stream().cuda_stream)
         _lib.check(st, "gemv_w4a16")
         return y
 

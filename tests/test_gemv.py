@@ -138,25 +138,20 @@ def test_config1_bf16_and_fp32_path(M):
 
 
 @pytest.mark.parametrize("M,K,N,G", [(1, 4096, 14336, 128), (3, 14336, 4096, 128), (16, 1024, 132, 64),
-                                     (2, 256, 4, 128), (1, 320, 1028, 64), (8, 8192, 8192, 256)])
+                                     (2, 256, 4, 128), (1, 320, 1024, 64), (8, 8192, 8192, 256),
+                                     (16, 14336, 4096, 128)])
 @pytest.mark.parametrize("act", ["f16", "bf16"])
-def test_stream_k_matches_oracle_and_cluster_path(M, K, N, G, act):
-    """The stream-K schedule (default) against the oracle and the cluster schedule;
-    shapes include fewer units than SMs, K not a multiple of a unit (320) and
-    tiles split across CTAs."""
+def test_heuristic_split_matches_oracle_and_fixed_splits(M, K, N, G, act):
+    """Default schedule vs the oracle and vs an explicit split count, including
+    tiny N, K that is not a multiple of the 8-row chunk per slice, and M=16 at
+    K=14336 where the split count is raised so activations fit on chip."""
     X, qw, ref = make_case(M, K, N, G, seed=M + K + N, act=act)
     ext = ng.extension()
     y = ext.gemv_w4a16(X, qw.qweight, qw.scales, G)
     check(y, ref, X.dtype)
-    yc = ext.gemv_w4a16(X, qw.qweight, qw.scales, G, splits_override=4)
+    yc = ext.gemv_w4a16(X, qw.qweight, qw.scales, G, splits_override=3)
     d = (y.float() - yc.float()).abs().max().item() / yc.float().abs().max().item()
     assert d < 4e-3
-    ws = ext.workspace(M, N, X.device, torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
-    n_tiles = (N + 127) // 128
-    sm = torch.cuda.get_device_properties(X.device).multi_processor_count
-    off = 2 * sm * 16 * 128 * 4  # counters follow the partial slots
-    assert int(ws[off: off + 4 * n_tiles].count_nonzero()) == 0, "tile counters must be left at zero"
     for _ in range(2):
         assert torch.equal(y, ext.gemv_w4a16(X, qw.qweight, qw.scales, G))
     assert ext.device_status() == 0
