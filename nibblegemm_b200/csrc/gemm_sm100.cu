@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (tile / n_tiles) * BT;
       const int acc = lt & 1;
       const uint32_t aph = (lt >> 1) & 1;
-      if (!warp_wait_bounded(&bars->tfull[acc], aph, err, abort)) break;
+      if (!mbar_wait_bounded(&bars->tfull[acc], aph, err, abort)) break;
       tc_fence_after();
       const int n = n0 + e * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(e * 32) << 16) + acc * BT;
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j + 1 < kPrefetch; ++j) pf[j] = pf[j + 1];
       pf[kPrefetch - 1] = scale_at(it + kPrefetch);
-      if (!warp_wait_bounded(&bars->full[s], ph, err, abort)) break;
+      if (!mbar_wait_bounded(&bars->full[s], ph, err, abort)) break;
       unsigned char* st = smem + s * kStageBytes;
       const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + kBTileBytes);
       unsigned char* arow = st + atom * 1024 + r8 * 128;

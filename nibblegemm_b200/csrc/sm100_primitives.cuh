@@ -36,10 +36,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "n"(20000)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -70,18 +70,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
       }
     }
   }
-}
-
-// Whole-warp wait: only lane 0 polls the barrier (so a waiting warp does not
-// put 32 lanes of mbarrier traffic on shared memory while TMA writes into it);
-// the outcome is broadcast and __syncwarp orders the other lanes after it.
-__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  unsigned int* err, volatile int* abort) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, err, abort) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
 }
 
 // ---------------------------------------------------------------------------
