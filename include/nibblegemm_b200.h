@@ -74,29 +74,45 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
                   int K, int N, int group_size, int fast, void* stream);
 
 /*
- * Decode-regime fused dequant GEMV, one launch, no workspace.
+ * Decode-regime fused dequant GEMV, one launch.
  * Replaces the reference's `gemv_w4a16(X, Wq, S, group_size, version,
  * splits_override, threads_override)` (csrc/gemv_w4a16.cu:341-425, bound at
- * csrc/bindings.cpp:12-15).  The reference reduces its K splits through an
- * fp32 workspace and a second kernel; here the CTAs of one column tile form a
- * thread-block cluster and reduce through distributed shared memory, in fixed
- * rank order (deterministic).
+ * csrc/bindings.cpp:12-15), which takes its split-K workspace from the torch
+ * caching allocator on every call; this one takes it from the caller.
  *   M in [1, 16]; N % 4 == 0; group_size in {64, 128, 256}; K % group_size == 0.
- *   splits: number of K slices (cluster size), 0 = heuristic, else 1..16; it
- *           is raised when needed so each slice's activations fit on chip.
- *   block_threads: 0 = heuristic (256), else 128 or 256.
- *   algo: 0 = default for the dtype; 1 = fp16 magic decode with packed-half2
- *         FMA windows of 32 values flushed to fp32 (fp16 x only);
- *         2 = fp32 magic decode with packed fp32x2 FMA, fp32 throughout.
- *         Default: 1 for fp16 x, 2 for bf16 x.
- *   Launched with programmatic stream serialisation: it starts streaming its
- *   (read-only) weights while the previous kernel on the stream finishes and
- *   reads x / writes y only after that kernel has completed.
+ *   Schedules:
+ *   - tensor pipe (default: algo 0 with splits == 0, block_threads == 0 and a
+ *     workspace; or algo 3): packed words decoded to magic-number fp16/bf16
+ *     operands of mma.sync, fp32 accumulation; persistent CTAs with equal
+ *     shares of (64-column tile, 128-value K slice) units; tiles split between
+ *     CTAs are finished by the last CTA to arrive, summing in CTA order
+ *     (deterministic).  `workspace`: ng_gemv_workspace_bytes(M, N) bytes,
+ *     256-byte aligned, zero-filled before first use; its layout does not
+ *     depend on M or N and each call leaves the part that must start at zero
+ *     (per-tile arrival counters) at zero.  Calls sharing a workspace must not
+ *     overlap on the GPU (one workspace per stream).
+ *   - CUDA-core cluster split-K (workspace == NULL, or algo 1 / 2, or
+ *     splits / block_threads given): `splits` K slices (1..16, 0 = heuristic,
+ *     raised if needed so a slice's activations fit on chip) reduced through
+ *     distributed shared memory inside a thread-block cluster, fixed rank
+ *     order; block_threads 0 (256), 128 or 256;  algo 1 = fp16 decode with
+ *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
+ *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x).
+ *   Both are launched with programmatic stream serialisation: they start
+ *   streaming their read-only weights while the previous kernel on the stream
+ *   finishes, and read x / write y / touch the workspace only after it has.
  *   x, qweight 16-byte aligned; scales 8-byte aligned.
  */
 int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
                   void* y, int M, int K, int N, int group_size, int splits, int block_threads,
-                  int algo, void* stream);
+                  int algo, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Workspace bytes the tensor-pipe GEMV needs for an N-column weight on the
+ * current device (0 if M or N is out of range).  No counterpart in the
+ * reference, which allocates its workspace inside each call.
+ */
+size_t ng_gemv_workspace_bytes(int M, int N);
 
 /*
  * Prefill-regime fused dequant GEMM on the sm_100 tensor cores: tcgen05.mma

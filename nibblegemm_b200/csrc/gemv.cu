@@ -383,7 +383,8 @@ int dispatch_w(int threads, const void* x, const uint32_t* qw, const __half* s, 
 
 extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
                              const uint16_t* scales, void* y, int M, int K, int N, int group_size,
-                             int splits, int block_threads, int algo, void* stream) {
+                             int splits, int block_threads, int algo, void* workspace,
+                             size_t workspace_bytes, void* stream) {
   using namespace ngb;
   if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
   if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
@@ -393,19 +394,35 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
   if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
   if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
-  if (algo < 0 || algo > 2) return NG_ERR_BAD_ARGUMENT;
+  if (algo < 0 || algo > 3) return NG_ERR_BAD_ARGUMENT;
   if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
-  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2) ||
+      !aligned(workspace, 256))
     return NG_ERR_MISALIGNED;
   DeviceInfo dev;
   if (int st = current_device_info(&dev)) return st;
   const auto* q = reinterpret_cast<const uint32_t*>(qweight);
   const auto* s = reinterpret_cast<const __half*>(scales);
   auto strm = static_cast<cudaStream_t>(stream);
+  const bool tensor_path = algo == 3 || (algo == 0 && splits == 0 && block_threads == 0);
+  if (tensor_path) {
+    if (workspace == nullptr) {
+      if (algo == 3) return NG_ERR_NULL_POINTER;
+    } else {
+      if (workspace_bytes < gemv_tc_workspace_bytes(N, dev)) return NG_ERR_BAD_ARGUMENT;
+      return gemv_tc(x, x_dtype, q, s, y, M, K, N, group_size, workspace, dev, strm);
+    }
+  }
   const int threads = block_threads ? block_threads : 256;
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_w<true, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
   if (algo == 2)
     return dispatch_w<false, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
   return dispatch_w<false, kHalf2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
+}
+
+extern "C" size_t ng_gemv_workspace_bytes(int M, int N) {
+  ngb::DeviceInfo dev;
+  if (M < 1 || M > 16 || N <= 0 || ngb::current_device_info(&dev) != NG_OK) return 0;
+  return ngb::gemv_tc_workspace_bytes(N, dev);
 }

@@ -127,6 +127,11 @@ int current_device_info(DeviceInfo* out);
 // opaque pointer; nullptr if unavailable.
 void* tensor_map_encode_fn();
 
+// Tensor-pipe decode GEMV (gemv_tc.cu); arguments already validated.
+size_t gemv_tc_workspace_bytes(int N, const DeviceInfo& dev);
+int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M, int K,
+            int N, int G, void* ws, const DeviceInfo& dev, cudaStream_t strm);
+
 
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

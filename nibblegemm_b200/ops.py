@@ -77,6 +77,22 @@ class _Extension:
 
     def __init__(self):
         self.lib = _lib.load()
+        self._ws = {}  # (device index, stream handle) -> zero-initialised GEMV workspace
+
+    def workspace(self, N: int, device: torch.device, stream: int) -> torch.Tensor:
+        """The decode-GEMV workspace for (device, stream), grown on demand.
+
+        Allocated zero-filled once; every call leaves its arrival counters at
+        zero, so it is reused as is (also across CUDA-graph replays).  One per
+        stream, because calls sharing a workspace must not overlap on the GPU.
+        """
+        need = self.lib.ng_gemv_workspace_bytes(1, N)
+        key = (device.index, stream)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 4 << 20), dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
 
     def dequant_w4(self, Wq: torch.Tensor, S: torch.Tensor, group_size: int, fast: bool = True,
                    out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
@@ -105,10 +121,12 @@ class _Extension:
         splits = 1 if version == 3 else int(splits_override)
         y = _out(out, M, N, X)
         with _on_device(X.device):
+            stream = torch.cuda.current_stream().cuda_stream
+            ws = self.workspace(N, X.device, stream)
             st = self.lib.ng_gemv_w4a16(X.data_ptr(), _DTYPE_CODE[X.dtype], Wq.data_ptr(),
                                         S.data_ptr(), y.data_ptr(), M, K, N, int(group_size), splits,
-                                        int(threads_override), int(algo),
-                                        torch.cuda.current_stream().cuda_stream)
+                                        int(threads_override), int(algo), ws.data_ptr(), ws.numel(),
+                                        stream)
         _lib.check(st, "gemv_w4a16")
         return y
 

@@ -64,7 +64,7 @@ FAKE = 0x1000  # a 16-byte-aligned non-null address; never dereferenced (validat
 def test_null_pointers_rejected():
     lib = _lib.load()
     c = status_codes()
-    assert lib.ng_gemv_w4a16(None, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_gemv_w4a16(None, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None, 0, None) == c["NG_ERR_NULL_POINTER"]
     assert lib.ng_gemm_w4a16(FAKE, 0, None, FAKE, FAKE, 32, 256, 128, 128, 0, None) == c["NG_ERR_NULL_POINTER"]
     assert lib.ng_dequant_w4(FAKE, None, FAKE, 0, 256, 128, 128, 1, None) == c["NG_ERR_NULL_POINTER"]
 
@@ -79,17 +79,17 @@ def test_null_pointers_rejected():
 ])
 def test_gemv_shape_validation(M, K, N, G):
     lib = _lib.load()
-    assert lib.ng_gemv_w4a16(FAKE, 0, FAKE, FAKE, FAKE, M, K, N, G, 0, 0, 0, None) == status_codes()["NG_ERR_BAD_SHAPE"]
+    assert lib.ng_gemv_w4a16(FAKE, 0, FAKE, FAKE, FAKE, M, K, N, G, 0, 0, 0, None, 0, None) == status_codes()["NG_ERR_BAD_SHAPE"]
 
 
 def test_gemv_option_validation():
     lib = _lib.load()
     c = status_codes()
-    assert lib.ng_gemv_w4a16(FAKE, 7, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None) == c["NG_ERR_BAD_DTYPE"]
-    assert lib.ng_gemv_w4a16(FAKE, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 17, 0, 0, None) == c["NG_ERR_BAD_ARGUMENT"]
-    assert lib.ng_gemv_w4a16(FAKE, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 96, 0, None) == c["NG_ERR_BAD_ARGUMENT"]
-    assert lib.ng_gemv_w4a16(FAKE, 1, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 1, None) == c["NG_ERR_BAD_ARGUMENT"]
-    assert lib.ng_gemv_w4a16(FAKE + 8, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None) == c["NG_ERR_MISALIGNED"]
+    assert lib.ng_gemv_w4a16(FAKE, 7, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None, 0, None) == c["NG_ERR_BAD_DTYPE"]
+    assert lib.ng_gemv_w4a16(FAKE, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 17, 0, 0, None, 0, None) == c["NG_ERR_BAD_ARGUMENT"]
+    assert lib.ng_gemv_w4a16(FAKE, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 96, 0, None, 0, None) == c["NG_ERR_BAD_ARGUMENT"]
+    assert lib.ng_gemv_w4a16(FAKE, 1, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 1, None, 0, None) == c["NG_ERR_BAD_ARGUMENT"]
+    assert lib.ng_gemv_w4a16(FAKE + 8, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None, 0, None) == c["NG_ERR_MISALIGNED"]
 
 
 def test_dequant_validation():

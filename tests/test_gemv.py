@@ -56,7 +56,7 @@ CASES = [(1, 512, 256), (2, 256, 132), (3, 1024, 260), (4, 512, 512), (5, 2048, 
 
 @pytest.mark.parametrize("M,K,N", CASES)
 @pytest.mark.parametrize("G", [64, 128])
-@pytest.mark.parametrize("act,algo", [("f16", 1), ("f16", 2), ("bf16", 0)])
+@pytest.mark.parametrize("act,algo", [("f16", 0), ("f16", 1), ("f16", 2), ("bf16", 0), ("bf16", 2)])
 def test_gemv_matches_oracle(M, K, N, G, act, algo):
     X, qw, ref = make_case(M, K, N, G, seed=M * 7 + N, act=act)
     y = ng.gemv(X, qw, algo=algo)
@@ -130,11 +130,25 @@ def test_full_size_shapes(K, N, M):
 
 
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
-def test_config1_bf16_and_fp32_path(M):
+def test_config1_every_path(M):
     X, qw, ref = make_case(M, 4096, 14336, 128, seed=11, act="bf16")
     check(ng.gemv(X, qw), ref, torch.bfloat16)
+    check(ng.gemv(X, qw, algo=2), ref, torch.bfloat16)
     X, qw, ref = make_case(M, 4096, 14336, 128, seed=12)
-    check(ng.gemv(X, qw, algo=2), ref, torch.float16)
+    for algo in (0, 1, 2, 3):
+        check(ng.gemv(X, qw, algo=algo), ref, torch.float16)
+
+
+def test_workspace_counters_left_zero():
+    ext = ng.extension()
+    for (M, K, N) in [(1, 4096, 14336), (16, 1024, 4100), (3, 14336, 4096)]:
+        X, qw, ref = make_case(M, K, N, 128, seed=N)
+        check(ext.gemv_w4a16(X, qw.qweight, qw.scales, 128), ref, torch.float16)
+        ws = ext.workspace(N, X.device, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        sm = torch.cuda.get_device_properties(X.device).multi_processor_count
+        off = 2 * 4 * sm * 16 * 64 * 4  # counters follow the partial-sum slots
+        assert int(ws[off:off + 4 * ((N + 63) // 64)].count_nonzero()) == 0
 
 
 @pytest.mark.parametrize("M,K,N,G", [(1, 4096, 14336, 128), (3, 14336, 4096, 128), (16, 1024, 132, 64),
