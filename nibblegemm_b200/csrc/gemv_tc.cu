@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   const int b = blockIdx.x;
   const long long u0 = part.start(b), u1 = part.start(b + 1);
   const long long n_my = u1 - u0;
-  const long long wu0 = u0 + n_my * warp / kWarps, wu1 = u0 + n_my * (warp + 1) / kWarps;
+  const long long wu0 = u0 + n_my * warp / kWarps, wu1 = u0 + n_my * (warp + 1) / kWarps;  // one-off 64-bit math
   const int tile_first = static_cast<int>(u0 / gpt);
   constexpr int UK = GS * 32;  // values of K per unit (64 or 128; a G = 256 group is two units)
 
@@ -130,20 +130,37 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   const uint64_t pol = make_evict_first_policy();
   uint4 wa[GS], wb[GS];
   uint2 sa[2], sb[2];
-  auto load_step = [&](long long u, int st) {
-    const int tile = static_cast<int>(u / gpt), sub = static_cast<int>(u % gpt);
-    const int ca = tile * kTN + 4 * g, cb = ca + 32;
-    const size_t r = static_cast<size_t>(sub) * (UK / 8) + t + st * 4;
-    wa[st] = ca < N ? ld_stream_v4(qw + r * N + ca, pol) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-    wb[st] = cb < N ? ld_stream_v4(qw + r * N + cb, pol) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+  const size_t rows4 = static_cast<size_t>(4) * N;  // 4 packed rows
+  // Addressing of one unit for this lane (all 32-bit index math but one
+  // 64-bit offset per unit; no divisions inside the loop).
+  struct Ptrs {
+    const uint32_t* a;
+    const uint32_t* b;
+    const __half* sa;
+    const __half* sb;
+    bool oka, okb;
   };
-  auto load_scales = [&](long long u, auto bufc) {
-    constexpr int B = decltype(bufc)::value;
-    const int tile = static_cast<int>(u / gpt), sub = static_cast<int>(u % gpt);
+  auto unit_ptrs = [&](int tile, int sub) {
+    Ptrs p;
     const int ca = tile * kTN + 4 * g, cb = ca + 32;
-    const size_t grp = (static_cast<size_t>(sub) * UK) / G;
-    sa[B] = ca < N ? ld_ro_v2(scales + grp * N + ca) : make_uint2(0u, 0u);
-    sb[B] = cb < N ? ld_ro_v2(scales + grp * N + cb) : make_uint2(0u, 0u);
+    p.oka = ca < N;
+    p.okb = cb < N;
+    p.a = qw + static_cast<size_t>(sub * (UK / 8) + t) * N + ca;
+    p.b = p.a + 32;
+    const size_t grp = static_cast<size_t>((sub * UK) / G);
+    p.sa = scales + grp * N + ca;
+    p.sb = p.sa + 32;
+    return p;
+  };
+  auto load_step = [&](const Ptrs& p, int st) {
+    const uint4 pad = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+    wa[st] = p.oka ? ld_stream_v4(p.a + st * rows4, pol) : pad;
+    wb[st] = p.okb ? ld_stream_v4(p.b + st * rows4, pol) : pad;
+  };
+  auto load_scales = [&](const Ptrs& p, auto bufc) {
+    constexpr int B = decltype(bufc)::value;
+    sa[B] = p.oka ? ld_ro_v2(p.sa) : make_uint2(0u, 0u);
+    sb[B] = p.okb ? ld_ro_v2(p.sb) : make_uint2(0u, 0u);
   };
 
   // zero the per-tile warp slots (this warp's own slots only)
@@ -175,9 +192,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
   int cur_tile = -1;
   constexpr uint32_t kMagic2 = XBF16 ? 0x43004300u : 0x64006400u;
-  auto process = [&](long long u, auto bufc) {
+  // Decode + MMA of one unit from the ring; refills each ring slot with the
+  // next unit's step as soon as it is consumed.
+  auto process = [&](int tile, int sub, bool has_next, const Ptrs& nxt, auto bufc) {
     constexpr int B = decltype(bufc)::value;
-    const int tile = static_cast<int>(u / gpt), sub = static_cast<int>(u % gpt);
     if (tile != cur_tile) {
       if (cur_tile >= 0) deposit(cur_tile);
       cur_tile = tile;
@@ -191,19 +209,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) c[i][nt][r] = 0.f;
       }
+    const unsigned short* xrow = x + static_cast<size_t>(g) * K + sub * UK + 8 * t;
 #pragma unroll
     for (int st = 0; st < GS; ++st) {
       // activations: rows m = nt*8 + g, k = sub*UK + st*32 + 8t .. +7
       uint4 xv[NT];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int m = nt * 8 + g;
-        xv[nt] = m < M ? ld_ro_v4(x + static_cast<size_t>(m) * K + static_cast<size_t>(sub) * UK + st * 32 + 8 * t)
-                       : make_uint4(0u, 0u, 0u, 0u);
-      }
+      for (int nt = 0; nt < NT; ++nt)
+        xv[nt] = nt * 8 + g < M ? ld_ro_v4(xrow + static_cast<size_t>(nt * 8) * K + st * 32)
+                                : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t wA[4] = {wa[st].x, wa[st].y, wa[st].z, wa[st].w};
       const uint32_t wB[4] = {wb[st].x, wb[st].y, wb[st].z, wb[st].w};
-      if (u + 1 < wu1) load_step(u + 1, st);  // slot st is free again
+      if (has_next) load_step(nxt, st);  // slot st is free again
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t ha[4], hb[4];
@@ -222,15 +239,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       }
     }
     // unit flush: tot += s * (c - corr * cv)
-    float fa[4], fb[4];
-    fa[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sa[B].x & 0xFFFF)));
-    fa[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sa[B].x >> 16)));
-    fa[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sa[B].y & 0xFFFF)));
-    fa[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sa[B].y >> 16)));
-    fb[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sb[B].x & 0xFFFF)));
-    fb[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sb[B].x >> 16)));
-    fb[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sb[B].y & 0xFFFF)));
-    fb[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sb[B].y >> 16)));
+    const __half2 ha01 = h2_from_bits(sa[B].x), ha23 = h2_from_bits(sa[B].y);
+    const __half2 hb01 = h2_from_bits(sb[B].x), hb23 = h2_from_bits(sb[B].y);
+    const float2 fa01 = __half22float2(ha01), fa23 = __half22float2(ha23);
+    const float2 fb01 = __half22float2(hb01), fb23 = __half22float2(hb23);
+    const float fa[4] = {fa01.x, fa01.y, fa23.x, fa23.y};
+    const float fb[4] = {fb01.x, fb01.y, fb23.x, fb23.y};
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       float corr[4];
@@ -246,18 +260,34 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
   using B0 = std::integral_constant<int, 0>;
   using B1 = std::integral_constant<int, 1>;
-  if (wu0 < wu1) {
+  const int nunits_w = static_cast<int>(wu1 - wu0);
+  int tile = static_cast<int>(wu0 / gpt), sub = static_cast<int>(wu0 % gpt);
+  auto advance = [&](int& tl, int& sb_) {
+    if (++sb_ == gpt) { sb_ = 0; ++tl; }
+  };
+  Ptrs cur = unit_ptrs(tile, sub);
+  if (nunits_w > 0) {
 #pragma unroll
-    for (int st = 0; st < GS; ++st) load_step(wu0, st);
-    load_scales(wu0, B0{});
+    for (int st = 0; st < GS; ++st) load_step(cur, st);
+    load_scales(cur, B0{});
   }
   griddep_wait();  // x, y and the workspace belong to the previous kernel until here
-  for (long long u = wu0; u < wu1; u += 2) {
-    if (u + 1 < wu1) load_scales(u + 1, B1{});
-    process(u, B0{});
-    if (u + 1 >= wu1) break;
-    if (u + 2 < wu1) load_scales(u + 2, B0{});
-    process(u + 1, B1{});
+  for (int k = 0; k < nunits_w; k += 2) {
+    int t1 = tile, s1 = sub;
+    advance(t1, s1);
+    const bool has1 = k + 1 < nunits_w;
+    const Ptrs p1 = unit_ptrs(t1, s1);
+    if (has1) load_scales(p1, B1{});
+    process(tile, sub, has1, p1, B0{});
+    if (!has1) break;
+    int t2 = t1, s2 = s1;
+    advance(t2, s2);
+    const bool has2 = k + 2 < nunits_w;
+    const Ptrs p2 = unit_ptrs(t2, s2);
+    if (has2) load_scales(p2, B0{});
+    process(t1, s1, has2, p2, B1{});
+    tile = t2;
+    sub = s2;
   }
   if (cur_tile >= 0) deposit(cur_tile);
   __syncthreads();
