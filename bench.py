@@ -185,6 +185,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gemv")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling target: run the op warmup+1 times eagerly on one GPU and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -219,6 +221,13 @@ def main():
         op = lambda i: ext.gemv_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G, out=Y)
     else:
         op = lambda i: ext.gemm_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G, out=Y)
+
+    if args.profile:  # a short, eager launch sequence for ncu -k ... -s <warmup> -c 1
+        for i in range(args.warmup + 1):
+            op(i)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_target": args.workload, "launches": args.warmup + 1}))
+        return
 
     # ---- device-timed region: K steps replayed from one CUDA graph ----------------
     stream = torch.cuda.Stream()

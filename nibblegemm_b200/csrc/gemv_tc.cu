@@ -86,16 +86,14 @@ __device__ __forceinline__ void decode_raw(uint32_t q, uint32_t (&h)[4]) {
   h[3] = and_or(q >> 12, 0x000F000Fu, kMagic);  // slots 3,7 -> k 6,7
 }
 
+// Balanced split of `units` work units over P CTAs: the first r CTAs get
+// q + 1 units, the rest q (q, r precomputed on the host) -- 32-bit math only.
 struct Part {
-  long long units;
-  int P;
-  __host__ __device__ long long start(int b) const { return static_cast<long long>(b) * units / P; }
-  __host__ __device__ int owner(long long u) const {
-    int b = static_cast<int>(((u + 1) * P - 1) / units);
-    if (b >= P) b = P - 1;
-    while (b + 1 < P && start(b + 1) <= u) ++b;
-    while (b > 0 && start(b) > u) --b;
-    return b;
+  int q, r;
+  __device__ __forceinline__ int start(int b) const { return b * q + min(b, r); }
+  __device__ __forceinline__ int owner(int u) const {
+    const int big = r * (q + 1);
+    return u < big ? u / (q + 1) : r + (u - big) / q;
   }
 };
 
@@ -103,7 +101,7 @@ template <int NT, int GS, bool XBF16>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     gemv_tc_kernel(const unsigned short* __restrict__ x, const uint32_t* __restrict__ qw,
                    const __half* __restrict__ scales, unsigned short* __restrict__ y, int M, int K,
-                   int N, int G, long long units, int gpt, float* __restrict__ partials,
+                   int N, int G, int part_q, int part_r, int gpt, float* __restrict__ partials,
                    unsigned int* __restrict__ counters) {
   constexpr int MR = NT * 8;              // rows of X covered
   constexpr int kSlot = MR * kTN;         // floats per (tile, warp) slot
@@ -114,12 +112,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const Part part{units, static_cast<int>(gridDim.x)};
+  const Part part{part_q, part_r};
   const int b = blockIdx.x;
-  const long long u0 = part.start(b), u1 = part.start(b + 1);
-  const long long n_my = u1 - u0;
-  const long long wu0 = u0 + n_my * warp / kWarps, wu1 = u0 + n_my * (warp + 1) / kWarps;  // one-off 64-bit math
-  const int tile_first = static_cast<int>(u0 / gpt);
+  const int u0 = part.start(b), u1 = part.start(b + 1);
+  const int n_my = u1 - u0;
+  const int wu0 = u0 + (n_my * warp) / kWarps, wu1 = u0 + (n_my * (warp + 1)) / kWarps;
+  const int tile_first = u0 / gpt;
   constexpr int UK = GS * 32;  // values of K per unit (64 or 128; a G = 256 group is two units)
 
   griddep_launch_dependents();
@@ -260,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 
   using B0 = std::integral_constant<int, 0>;
   using B1 = std::integral_constant<int, 1>;
-  const int nunits_w = static_cast<int>(wu1 - wu0);
-  int tile = static_cast<int>(wu0 / gpt), sub = static_cast<int>(wu0 % gpt);
+  const int nunits_w = wu1 - wu0;
+  int tile = wu0 / gpt, sub = wu0 - (wu0 / gpt) * gpt;
   auto advance = [&](int& tl, int& sb_) {
     if (++sb_ == gpt) { sb_ = 0; ++tl; }
   };
@@ -293,9 +291,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   __syncthreads();
 
   // ---- per-tile reduction over warps (warp order), emit or hand off -----------
-  const int tile_last = n_my > 0 ? static_cast<int>((u1 - 1) / gpt) : tile_first - 1;
+  const int tile_last = n_my > 0 ? (u1 - 1) / gpt : tile_first - 1;
   for (int tile = tile_first; tile <= tile_last; ++tile) {
-    const long long tu0 = static_cast<long long>(tile) * gpt, tu1 = tu0 + gpt;
+    const int tu0 = tile * gpt, tu1 = tu0 + gpt;
     const bool whole = tu0 >= u0 && tu1 <= u1;
     const float* base = red + (tile - tile_first) * kWarps * kSlot;
     const int slot = 2 * b + (tile == tile_first ? 0 : 1);
@@ -326,8 +324,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       for (int e = threadIdx.x; e < kSlot; e += kThreads) {
         float v = 0.f;
         for (int bb = bf; bb <= bl; ++bb) {
-          const int tf = static_cast<int>(part.start(bb) / gpt);
-          const int sl = 2 * bb + (tile == tf ? 0 : 1);
+          // contributor bb wrote this tile to its first slot iff the tile is
+          // the first one of its range
+          const int sl = 2 * bb + (part.start(bb) >= tu0 ? 0 : 1);
           v += __ldcg(&partials[static_cast<size_t>(sl) * (kMaxM * kTN) + e]);
         }
         const int m = e / kTN, n = tile * kTN + (e % kTN);
@@ -368,6 +367,7 @@ int run_tc(const void* x, const uint32_t* q, const __half* s, void* y, int M, in
   const int tiles = (N + kTN - 1) / kTN;
   const int gpt = K / (GS * 32);  // units per tile
   const long long units = static_cast<long long>(tiles) * gpt;
+  if (units >= (1LL << 30)) return NG_ERR_BAD_SHAPE;
   // All CTAs resident; enough CTAs that a range touches at most kMaxTiles tiles.
   long long P = static_cast<long long>(dev.sm_count) * resident[dev.device];
   P = std::max<long long>(P, (tiles + kMaxTiles - 3) / (kMaxTiles - 2));
@@ -386,8 +386,9 @@ int run_tc(const void* x, const uint32_t* q, const __half* s, void* y, int M, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const int pq = static_cast<int>(units / P), pr = static_cast<int>(units % P);
   return launch_status(cudaLaunchKernelEx(&cfg, kern, static_cast<const unsigned short*>(x), q, s,
-                                          static_cast<unsigned short*>(y), M, K, N, G, units, gpt,
+                                          static_cast<unsigned short*>(y), M, K, N, G, pq, pr, gpt,
                                           partials, counters));
 }
 
