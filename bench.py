@@ -185,6 +185,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gemv")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--algo", type=int, default=0, help="GEMV schedule (see ng_gemv_w4a16)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: run the op warmup+1 times eagerly on one GPU and exit")
     args = ap.parse_args()
@@ -218,7 +219,8 @@ def main():
     Y = torch.empty(M, N, dtype=torch.float16, device="cuda")
     ext = ng.extension()
     if args.workload == "gemv":
-        op = lambda i: ext.gemv_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G, out=Y)
+        op = lambda i: ext.gemv_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G,
+                                      algo=args.algo, out=Y)
     else:
         op = lambda i: ext.gemm_w4a16(X, qw_dev[i % nrot].qweight, qw_dev[i % nrot].scales, G, out=Y)
 

@@ -81,8 +81,7 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  * caching allocator on every call; this one takes it from the caller.
  *   M in [1, 16]; N % 4 == 0; group_size in {64, 128, 256}; K % group_size == 0.
  *   Schedules:
- *   - tensor pipe (default: algo 0 with splits == 0, block_threads == 0 and a
- *     workspace; or algo 3): packed words decoded to magic-number fp16/bf16
+ *   - tensor pipe (algo 3; needs the workspace): packed words decoded to magic-number fp16/bf16
  *     operands of mma.sync, fp32 accumulation; persistent CTAs with equal
  *     shares of (64-column tile, 128-value K slice) units; tiles split between
  *     CTAs are finished by the last CTA to arrive, summing in CTA order
@@ -91,13 +90,14 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     depend on M or N and each call leaves the part that must start at zero
  *     (per-tile arrival counters) at zero.  Calls sharing a workspace must not
  *     overlap on the GPU (one workspace per stream).
- *   - CUDA-core cluster split-K (workspace == NULL, or algo 1 / 2, or
- *     splits / block_threads given): `splits` K slices (1..16, 0 = heuristic,
+ *   - CUDA-core cluster split-K (default, algo 0 / 1 / 2; the workspace is
+ *     not used): `splits` K slices (1..16, 0 = heuristic,
  *     raised if needed so a slice's activations fit on chip) reduced through
  *     distributed shared memory inside a thread-block cluster, fixed rank
  *     order; block_threads 0 (256), 128 or 256;  algo 1 = fp16 decode with
  *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
- *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x).
+ *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x);
+ *     algo 0 = 1 for fp16 x, 2 for bf16 x.
  *   Both are launched with programmatic stream serialisation: they start
  *   streaming their read-only weights while the previous kernel on the stream
  *   finishes, and read x / write y / touch the workspace only after it has.

@@ -404,7 +404,7 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   const auto* q = reinterpret_cast<const uint32_t*>(qweight);
   const auto* s = reinterpret_cast<const __half*>(scales);
   auto strm = static_cast<cudaStream_t>(stream);
-  const bool tensor_path = algo == 3 || (algo == 0 && splits == 0 && block_threads == 0);
+  const bool tensor_path = algo == 3;
   if (tensor_path) {
     if (workspace == nullptr) {
       if (algo == 3) return NG_ERR_NULL_POINTER;
