@@ -97,18 +97,44 @@ struct Part {
   }
 };
 
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kRing = 2;  // units of weights in flight per warp (shared-memory ring)
+constexpr int kWarpSlots = 3;  // distinct tiles one warp's range may touch
+
+template <int NT, int GS>
+struct TcSmem {
+  static constexpr int kSlot = NT * 8 * kTN;                       // floats per warp-tile partial
+  static constexpr int kRingBytes = kWarps * kRing * GS * 2 * 32 * 16;
+  static constexpr int kRedBytes = kWarps * kWarpSlots * kSlot * 4;
+  static constexpr int kBytes = kRingBytes + kRedBytes;
+};
+
 template <int NT, int GS, bool XBF16>
 __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
     gemv_tc_kernel(const unsigned short* __restrict__ x, const uint32_t* __restrict__ qw,
                    const __half* __restrict__ scales, unsigned short* __restrict__ y, int M, int K,
                    int N, int G, int part_q, int part_r, int gpt, float* __restrict__ partials,
-                   unsigned int* __restrict__ counters) {
-  constexpr int MR = NT * 8;              // rows of X covered
-  constexpr int kSlot = MR * kTN;         // floats per (tile, warp) slot
+                   unsigned int* __restrict__ counters, unsigned int* __restrict__ err) {
+  using L = TcSmem<NT, GS>;
+  constexpr int kSlot = L::kSlot;
+  constexpr int UK = GS * 32;  // values of K per unit (64 or 128; a G = 256 group is two units)
   // (magic + 8) / magic: removes the magic offset and the zero point at once.
   constexpr float kCorr = XBF16 ? (136.0f / 128.0f) : (1032.0f / 1024.0f);
-  extern __shared__ __align__(16) float red[];  // [kMaxTiles][kWarps][MR][kTN]
-  __shared__ int s_last;
+  constexpr uint32_t kMagic2 = XBF16 ? 0x43004300u : 0x64006400u;
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint4* ring = reinterpret_cast<uint4*>(smem);                       // [warp][kRing][GS*2][32]
+  float* red = reinterpret_cast<float*>(smem + L::kRingBytes);         // [warp][kWarpSlots][kSlot]
+  __shared__ int s_arrive[kMaxTiles];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -116,54 +142,110 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
   const int b = blockIdx.x;
   const int u0 = part.start(b), u1 = part.start(b + 1);
   const int n_my = u1 - u0;
-  const int wu0 = u0 + (n_my * warp) / kWarps, wu1 = u0 + (n_my * (warp + 1)) / kWarps;
+  auto wstart = [&](int w) { return u0 + (n_my * w) / kWarps; };
+  const int wu0 = wstart(warp), wu1 = wstart(warp + 1);
   const int tile_first = u0 / gpt;
-  constexpr int UK = GS * 32;  // values of K per unit (64 or 128; a G = 256 group is two units)
+  const int my_first_tile = wu0 / gpt;
+  if (threadIdx.x < kMaxTiles) s_arrive[threadIdx.x] = 0;
 
   griddep_launch_dependents();
 
-  // ---- weight ring: one slot per step of a unit (GS x 2 x 16 B per lane).  Slot
-  // st of the next unit is refilled as soon as step st of the current one is
-  // decoded, so GS steps stay in flight per warp at all times.
-  const uint64_t pol = make_evict_first_policy();
-  uint4 wa[GS], wb[GS];
-  uint2 sa[2], sb[2];
+  // ---- addressing of one unit for this lane -------------------------------------
   const size_t rows4 = static_cast<size_t>(4) * N;  // 4 packed rows
-  // Addressing of one unit for this lane (all 32-bit index math but one
-  // 64-bit offset per unit; no divisions inside the loop).
-  struct Ptrs {
-    const uint32_t* a;
-    const uint32_t* b;
-    const __half* sa;
-    const __half* sb;
-    bool oka, okb;
-  };
-  auto unit_ptrs = [&](int tile, int sub) {
-    Ptrs p;
+  auto issue_unit = [&](int tile, int sub, int d) {
     const int ca = tile * kTN + 4 * g, cb = ca + 32;
-    p.oka = ca < N;
-    p.okb = cb < N;
-    p.a = qw + static_cast<size_t>(sub * (UK / 8) + t) * N + ca;
-    p.b = p.a + 32;
+    const uint32_t* pa = qw + static_cast<size_t>(sub * (UK / 8) + t) * N + ca;
+    uint4* dst = ring + ((warp * kRing + d) * (GS * 2)) * 32 + lane;
+#pragma unroll
+    for (int st = 0; st < GS; ++st) {
+      cp_async_16(dst + (2 * st) * 32, ca < N ? pa + st * rows4 : qw, ca < N);
+      cp_async_16(dst + (2 * st + 1) * 32, cb < N ? pa + 32 + st * rows4 : qw, cb < N);
+    }
+  };
+  auto load_scales = [&](int tile, int sub, uint2& sa, uint2& sb) {
+    const int ca = tile * kTN + 4 * g, cb = ca + 32;
     const size_t grp = static_cast<size_t>((sub * UK) / G);
-    p.sa = scales + grp * N + ca;
-    p.sb = p.sa + 32;
-    return p;
+    sa = ca < N ? ld_ro_v2(scales + grp * N + ca) : make_uint2(0u, 0u);
+    sb = cb < N ? ld_ro_v2(scales + grp * N + cb) : make_uint2(0u, 0u);
   };
-  auto load_step = [&](const Ptrs& p, int st) {
-    const uint4 pad = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-    wa[st] = p.oka ? ld_stream_v4(p.a + st * rows4, pol) : pad;
-    wb[st] = p.okb ? ld_stream_v4(p.b + st * rows4, pol) : pad;
-  };
-  auto load_scales = [&](const Ptrs& p, auto bufc) {
-    constexpr int B = decltype(bufc)::value;
-    sa[B] = p.oka ? ld_ro_v2(p.sa) : make_uint2(0u, 0u);
-    sb[B] = p.okb ? ld_ro_v2(p.sb) : make_uint2(0u, 0u);
+  auto load_x = [&](int sub, uint4 (&xv)[GS][NT]) {
+    const unsigned short* xrow = x + static_cast<size_t>(g) * K + sub * UK + 8 * t;
+#pragma unroll
+    for (int st = 0; st < GS; ++st)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        xv[st][nt] = nt * 8 + g < M ? ld_ro_v4(xrow + static_cast<size_t>(nt * 8) * K + st * 32)
+                                    : make_uint4(0u, 0u, 0u, 0u);
   };
 
-  // zero the per-tile warp slots (this warp's own slots only)
-  for (int i = lane; i < kMaxTiles * kSlot; i += 32)
-    red[(i / kSlot) * kWarps * kSlot + warp * kSlot + (i % kSlot)] = 0.f;
+  // Number of warps of this CTA whose range touches `tile` (contiguous split).
+  auto warps_on_tile = [&](int tile) {
+    int n = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const int a0 = wstart(w), a1 = wstart(w + 1);
+      n += (a0 < a1 && a0 < (tile + 1) * gpt && a1 > tile * gpt) ? 1 : 0;
+    }
+    return n;
+  };
+
+  // The last warp of this CTA to finish its part of `tile` reduces the warps'
+  // partials (in warp order) and then: writes Y (tile entirely in this CTA's
+  // range), publishes a partial (the tile began in an earlier CTA's range:
+  // that CTA finishes it), or waits for the later CTAs' partials and finishes
+  // the tile (it owns the tile's first unit) -- deterministic in every case.
+  auto finish_tile = [&](int tile) {
+    const int tu0 = tile * gpt, tu1 = tu0 + gpt;
+    const bool starts_here = tu0 >= u0;
+    const bool ends_here = tu1 <= u1;
+    const int bl = ends_here ? b : part.owner(tu1 - 1);
+    if (starts_here && bl > b) {
+      // finisher: wait (bounded) until every later contributor has published
+      if (lane == 0) {
+        const unsigned int need = static_cast<unsigned int>(bl - b);
+        const uint64_t t0 = global_timer_ns();
+        unsigned int v;
+        for (;;) {
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counters + tile) : "memory");
+          if (v >= need) break;
+          if (global_timer_ns() - t0 > 1000000000ull) {
+            atomicOr(err, kErrWaitTimeout);
+            break;
+          }
+        }
+      }
+      __syncwarp();
+      __threadfence();
+    }
+    for (int e = lane; e < kSlot; e += 32) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const int a0 = wstart(w), a1 = wstart(w + 1);
+        if (a0 < a1 && a0 < tu1 && a1 > tu0)
+          v += red[(w * kWarpSlots + (tile - a0 / gpt)) * kSlot + e];
+      }
+      if (!starts_here) {
+        partials[static_cast<size_t>(b) * (kMaxM * kTN) + e] = v;
+        continue;
+      }
+      for (int bb = b + 1; bb <= bl; ++bb)
+        v += __ldcg(&partials[static_cast<size_t>(bb) * (kMaxM * kTN) + e]);
+      const int m = e / kTN, n = tile * kTN + (e % kTN);
+      if (m < M && n < N)
+        y[static_cast<size_t>(m) * N + n] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                  : __half_as_ushort(__float2half_rn(v));
+    }
+    if (!starts_here) {
+      __threadfence();
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counters + tile) : "memory");
+    } else if (bl > b) {
+      __syncwarp();
+      if (lane == 0) counters[tile] = 0u;  // every contributor has arrived: reset for the next call
+    }
+  };
 
   float tot[4][NT][4];
 #pragma unroll
@@ -174,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
       for (int r = 0; r < 4; ++r) tot[i][nt][r] = 0.f;
 
   auto deposit = [&](int tile) {
-    float* slot = red + ((tile - tile_first) * kWarps + warp) * kSlot;
+    float* slot = red + (warp * kWarpSlots + (tile - my_first_tile)) * kSlot;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -186,18 +268,54 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
           slot[m * kTN + c] = tot[i][nt][r];
           tot[i][nt][r] = 0.f;
         }
+    __threadfence_block();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&s_arrive[tile - tile_first], 1) == warps_on_tile(tile) - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence_block();
+      finish_tile(tile);
+    }
   };
 
+  // ---- main loop ---------------------------------------------------------------
+  const int nw = wu1 - wu0;
+  int tile = wu0 / gpt, sub = wu0 - (wu0 / gpt) * gpt;
+  // weights for the first kRing units go out before the dependency wait
+  {
+    int tl = tile, sb = sub;
+#pragma unroll
+    for (int d = 0; d < kRing; ++d) {
+      if (d < nw) issue_unit(tl, sb, d);
+      cp_async_commit();
+      if (++sb == gpt) { sb = 0; ++tl; }
+    }
+  }
+  __syncthreads();  // s_arrive initialised
+  griddep_wait();   // x, y and the workspace belong to the previous kernel until here
+
+  uint4 xv[2][GS][NT];
+  uint2 sa[2], sb2[2];
+  if (nw > 0) {
+    load_x(sub, xv[0]);
+    load_scales(tile, sub, sa[0], sb2[0]);
+  }
   int cur_tile = -1;
-  constexpr uint32_t kMagic2 = XBF16 ? 0x43004300u : 0x64006400u;
-  // Decode + MMA of one unit from the ring; refills each ring slot with the
-  // next unit's step as soon as it is consumed.
-  auto process = [&](int tile, int sub, bool has_next, const Ptrs& nxt, auto bufc) {
+  auto process = [&](int k, auto bufc) {
     constexpr int B = decltype(bufc)::value;
     if (tile != cur_tile) {
       if (cur_tile >= 0) deposit(cur_tile);
       cur_tile = tile;
     }
+    int nt_tile = tile, nt_sub = sub;
+    if (++nt_sub == gpt) { nt_sub = 0; ++nt_tile; }
+    if (k + 1 < nw) {  // next unit's activations and scales into the other register buffer
+      load_x(nt_sub, xv[B ^ 1]);
+      load_scales(nt_tile, nt_sub, sa[B ^ 1], sb2[B ^ 1]);
+    }
+    cp_async_wait<kRing - 1>();  // this unit's weights have landed (this lane's own copies)
+    const uint4* src = ring + ((warp * kRing + (k % kRing)) * (GS * 2)) * 32 + lane;
     float c[4][NT][4], cv[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -207,18 +325,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) c[i][nt][r] = 0.f;
       }
-    const unsigned short* xrow = x + static_cast<size_t>(g) * K + sub * UK + 8 * t;
+    uint32_t consumed = 0;  // ties the ring refill below to the completion of these reads
 #pragma unroll
     for (int st = 0; st < GS; ++st) {
-      // activations: rows m = nt*8 + g, k = sub*UK + st*32 + 8t .. +7
-      uint4 xv[NT];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        xv[nt] = nt * 8 + g < M ? ld_ro_v4(xrow + static_cast<size_t>(nt * 8) * K + st * 32)
-                                : make_uint4(0u, 0u, 0u, 0u);
-      const uint32_t wA[4] = {wa[st].x, wa[st].y, wa[st].z, wa[st].w};
-      const uint32_t wB[4] = {wb[st].x, wb[st].y, wb[st].z, wb[st].w};
-      if (has_next) load_step(nxt, st);  // slot st is free again
+      const uint4 qa = src[(2 * st) * 32], qb = src[(2 * st + 1) * 32];
+      consumed ^= qa.x ^ qb.x;
+      const uint32_t wA[4] = {qa.x, qa.y, qa.z, qa.w};
+      const uint32_t wB[4] = {qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t ha[4], hb[4];
@@ -226,21 +339,31 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
         decode_raw<XBF16>(wB[i], hb);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          mma16816<XBF16>(c[i][nt], ha[0], hb[0], ha[1], hb[1], xv[nt].x, xv[nt].y);
-          mma16816<XBF16>(c[i][nt], ha[2], hb[2], ha[3], hb[3], xv[nt].z, xv[nt].w);
+          mma16816<XBF16>(c[i][nt], ha[0], hb[0], ha[1], hb[1], xv[B][st][nt].x, xv[B][st][nt].y);
+          mma16816<XBF16>(c[i][nt], ha[2], hb[2], ha[3], hb[3], xv[B][st][nt].z, xv[B][st][nt].w);
         }
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        mma16816<XBF16>(cv[nt], kMagic2, kMagic2, kMagic2, kMagic2, xv[nt].x, xv[nt].y);
-        mma16816<XBF16>(cv[nt], kMagic2, kMagic2, kMagic2, kMagic2, xv[nt].z, xv[nt].w);
+        mma16816<XBF16>(cv[nt], kMagic2, kMagic2, kMagic2, kMagic2, xv[B][st][nt].x, xv[B][st][nt].y);
+        mma16816<XBF16>(cv[nt], kMagic2, kMagic2, kMagic2, kMagic2, xv[B][st][nt].z, xv[B][st][nt].w);
       }
     }
+    // ring slot consumed: refill it with the unit kRing ahead.  The empty asm
+    // takes the values read from the slot as inputs, so the copies that
+    // overwrite it are issued only after those reads have returned.
+    asm volatile("" ::"r"(consumed) : "memory");
+    {
+      int tl = tile, sb = sub;
+#pragma unroll
+      for (int d = 0; d < kRing; ++d)
+        if (++sb == gpt) { sb = 0; ++tl; }
+      if (k + kRing < nw) issue_unit(tl, sb, k % kRing);
+      cp_async_commit();
+    }
     // unit flush: tot += s * (c - corr * cv)
-    const __half2 ha01 = h2_from_bits(sa[B].x), ha23 = h2_from_bits(sa[B].y);
-    const __half2 hb01 = h2_from_bits(sb[B].x), hb23 = h2_from_bits(sb[B].y);
-    const float2 fa01 = __half22float2(ha01), fa23 = __half22float2(ha23);
-    const float2 fb01 = __half22float2(hb01), fb23 = __half22float2(hb23);
+    const float2 fa01 = __half22float2(h2_from_bits(sa[B].x)), fa23 = __half22float2(h2_from_bits(sa[B].y));
+    const float2 fb01 = __half22float2(h2_from_bits(sb2[B].x)), fb23 = __half22float2(h2_from_bits(sb2[B].y));
     const float fa[4] = {fa01.x, fa01.y, fa23.x, fa23.y};
     const float fb[4] = {fb01.x, fb01.y, fb23.x, fb23.y};
 #pragma unroll
@@ -254,108 +377,36 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
         for (int r = 0; r < 4; ++r)
           tot[i][nt][r] = fmaf(r < 2 ? fa[i] : fb[i], c[i][nt][r] - corr[r], tot[i][nt][r]);
     }
+    tile = nt_tile;
+    sub = nt_sub;
   };
-
   using B0 = std::integral_constant<int, 0>;
   using B1 = std::integral_constant<int, 1>;
-  const int nunits_w = wu1 - wu0;
-  int tile = wu0 / gpt, sub = wu0 - (wu0 / gpt) * gpt;
-  auto advance = [&](int& tl, int& sb_) {
-    if (++sb_ == gpt) { sb_ = 0; ++tl; }
-  };
-  Ptrs cur = unit_ptrs(tile, sub);
-  if (nunits_w > 0) {
-#pragma unroll
-    for (int st = 0; st < GS; ++st) load_step(cur, st);
-    load_scales(cur, B0{});
-  }
-  griddep_wait();  // x, y and the workspace belong to the previous kernel until here
-  for (int k = 0; k < nunits_w; k += 2) {
-    int t1 = tile, s1 = sub;
-    advance(t1, s1);
-    const bool has1 = k + 1 < nunits_w;
-    const Ptrs p1 = unit_ptrs(t1, s1);
-    if (has1) load_scales(p1, B1{});
-    process(tile, sub, has1, p1, B0{});
-    if (!has1) break;
-    int t2 = t1, s2 = s1;
-    advance(t2, s2);
-    const bool has2 = k + 2 < nunits_w;
-    const Ptrs p2 = unit_ptrs(t2, s2);
-    if (has2) load_scales(p2, B0{});
-    process(t1, s1, has2, p2, B1{});
-    tile = t2;
-    sub = s2;
+  for (int k = 0; k < nw; k += 2) {
+    process(k, B0{});
+    if (k + 1 >= nw) break;
+    process(k + 1, B1{});
   }
   if (cur_tile >= 0) deposit(cur_tile);
-  __syncthreads();
-
-  // ---- per-tile reduction over warps (warp order), emit or hand off -----------
-  const int tile_last = n_my > 0 ? (u1 - 1) / gpt : tile_first - 1;
-  for (int tile = tile_first; tile <= tile_last; ++tile) {
-    const int tu0 = tile * gpt, tu1 = tu0 + gpt;
-    const bool whole = tu0 >= u0 && tu1 <= u1;
-    const float* base = red + (tile - tile_first) * kWarps * kSlot;
-    const int slot = 2 * b + (tile == tile_first ? 0 : 1);
-    for (int e = threadIdx.x; e < kSlot; e += kThreads) {
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) v += base[w * kSlot + e];
-      const int m = e / kTN, n = tile * kTN + (e % kTN);
-      if (whole) {
-        if (m < M && n < N)
-          y[static_cast<size_t>(m) * N + n] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
-                                                    : __half_as_ushort(__float2half_rn(v));
-      } else {
-        partials[static_cast<size_t>(slot) * (kMaxM * kTN) + e] = v;
-      }
-    }
-    if (whole) continue;
-    __threadfence();
-    __syncthreads();
-    const int bf = part.owner(tu0), bl = part.owner(tu1 - 1);
-    if (threadIdx.x == 0) {
-      const unsigned int prev = atomicAdd(&counters[tile], 1u);
-      s_last = (prev == static_cast<unsigned int>(bl - bf));
-    }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      for (int e = threadIdx.x; e < kSlot; e += kThreads) {
-        float v = 0.f;
-        for (int bb = bf; bb <= bl; ++bb) {
-          // contributor bb wrote this tile to its first slot iff the tile is
-          // the first one of its range
-          const int sl = 2 * bb + (part.start(bb) >= tu0 ? 0 : 1);
-          v += __ldcg(&partials[static_cast<size_t>(sl) * (kMaxM * kTN) + e]);
-        }
-        const int m = e / kTN, n = tile * kTN + (e % kTN);
-        if (m < M && n < N)
-          y[static_cast<size_t>(m) * N + n] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
-                                                    : __half_as_ushort(__float2half_rn(v));
-      }
-      if (threadIdx.x == 0) counters[tile] = 0u;
-    }
-    __syncthreads();
-  }
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-// Workspace: partial-sum slots (2 per CTA, up to 4 CTAs per SM, 16 x 64 floats
-// each) followed by one arrival counter per 64-column tile.  The layout does
-// not depend on M; only the counters must be zero between calls and every
-// call leaves them zero.
+// Workspace: one partial-sum slot per CTA (up to 4 CTAs per SM, 16 x 64
+// floats each) followed by one arrival counter per 64-column tile.  The layout
+// does not depend on M; only the counters must be zero between calls and
+// every call leaves them zero.
 size_t tc_counter_offset(int sm_count) {
-  return static_cast<size_t>(2) * 4 * sm_count * kMaxM * kTN * sizeof(float);
+  return static_cast<size_t>(4) * sm_count * kMaxM * kTN * sizeof(float);
 }
 
 template <int NT, int GS, bool XBF16>
 int run_tc(const void* x, const uint32_t* q, const __half* s, void* y, int M, int K, int N, int G,
            void* ws, const DeviceInfo& dev, cudaStream_t stream) {
   auto kern = gemv_tc_kernel<NT, GS, XBF16>;
-  constexpr size_t smem = static_cast<size_t>(kMaxTiles) * kWarps * NT * 8 * kTN * sizeof(float);
+  constexpr size_t smem = TcSmem<NT, GS>::kBytes;
   static std::once_flag once[64];
   static int resident[64];
   std::call_once(once[dev.device], [&] {
@@ -368,11 +419,13 @@ int run_tc(const void* x, const uint32_t* q, const __half* s, void* y, int M, in
   const int gpt = K / (GS * 32);  // units per tile
   const long long units = static_cast<long long>(tiles) * gpt;
   if (units >= (1LL << 30)) return NG_ERR_BAD_SHAPE;
-  // All CTAs resident; enough CTAs that a range touches at most kMaxTiles tiles.
-  long long P = static_cast<long long>(dev.sm_count) * resident[dev.device];
-  P = std::max<long long>(P, (tiles + kMaxTiles - 3) / (kMaxTiles - 2));
-  P = std::min<long long>(P, units);
-  if (P > 4LL * dev.sm_count) return NG_ERR_BAD_SHAPE;
+  // Every CTA resident at once (the finisher of a split tile waits for the
+  // later CTAs; a cooperative launch guarantees they are running).  A CTA's
+  // range must touch at most kMaxTiles tiles and a warp's at most kWarpSlots.
+  const long long P = std::min<long long>(static_cast<long long>(dev.sm_count) * resident[dev.device], units);
+  const long long per_cta = (units + P - 1) / P;
+  if ((per_cta + gpt - 1) / gpt + 1 > kMaxTiles) return NG_ERR_BAD_SHAPE;
+  if ((per_cta / kWarps + 1 + gpt - 1) / gpt + 1 > kWarpSlots) return NG_ERR_BAD_SHAPE;
   auto* partials = static_cast<float*>(ws);
   auto* counters = reinterpret_cast<unsigned int*>(static_cast<unsigned char*>(ws) +
                                                    tc_counter_offset(dev.sm_count));
@@ -381,15 +434,17 @@ int run_tc(const void* x, const uint32_t* q, const __half* s, void* y, int M, in
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const int pq = static_cast<int>(units / P), pr = static_cast<int>(units % P);
   return launch_status(cudaLaunchKernelEx(&cfg, kern, static_cast<const unsigned short*>(x), q, s,
                                           static_cast<unsigned short*>(y), M, K, N, G, pq, pr, gpt,
-                                          partials, counters));
+                                          partials, counters, dev.err));
 }
 
 }  // namespace
