@@ -115,6 +115,28 @@ int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint
 size_t ng_gemv_workspace_bytes(int M, int N);
 
 /*
+ * Allocation-free variant of the tensor-pipe GEMV (ng_gemv_w4a16, algo 3).
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory at the point of the call (code inside an allocator or memory
+ * hook, plugins whose host owns all allocation, allocation-free inference
+ * loops) and so cannot supply a workspace.  The scratch space comes from a
+ * fixed 3 MiB array in the library's device data, present on every GPU that
+ * loads the library until the process exits.
+ *   Same arguments and limits as ng_gemv_w4a16 otherwise; returns
+ *   NG_ERR_BAD_SHAPE when the shape needs more scratch than the array holds
+ *   (about N > 8 million columns on a 148-SM B200).
+ *   The first call on a device looks up the array's device address (with that
+ *   device current); make that first call before any stream capture.
+ *   Each call clears the array's arrival counters on `stream` before the
+ *   kernel (cudaMemsetAsync; nothing is allocated).  All calls on a device
+ *   share the one array: calls that overlap on the GPU (different streams,
+ *   concurrent graphs) race and must be serialised by the caller.
+ */
+int ng_gemv_w4a16_noalloc(const void* x, int x_dtype, const int32_t* qweight,
+                          const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                          void* stream);
+
+/*
  * Prefill-regime fused dequant GEMM on the sm_100 tensor cores: tcgen05.mma
  * with accumulators in tensor memory, activations staged by TMA, weight tiles
  * decoded by CUDA-core warps straight into the tensor cores' shared-memory

@@ -26,6 +26,7 @@ SIGNATURES = {
     "ng_dequant_w4": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "ng_gemv_w4a16": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P]),
     "ng_gemv_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
+    "ng_gemv_w4a16_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ng_gemm_w4a16": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
 }
 

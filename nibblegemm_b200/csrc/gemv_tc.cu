@@ -469,3 +469,69 @@ int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void
 }
 
 }  // namespace ngb
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory when they call the GEMV: code
+// running inside a host allocator's or a framework's own memory hook (where a
+// cudaMalloc would re-enter it), plugins whose host owns every allocation and
+// hands out none, and inference loops that must not touch the allocator on the
+// critical path.  They cannot provide the tensor-pipe GEMV's workspace, so this
+// entry point takes it from a fixed array in the library's device data
+// instead.  The array exists once per GPU that loads the library and stays
+// allocated until the process exits.
+// ---------------------------------------------------------------------------
+namespace ngb {
+namespace {
+
+// 3 MiB: partial-sum slots for up to 4 CTAs per SM on up to 160 SMs (2.5 MiB)
+// plus arrival counters for ~131k 64-column tiles.
+constexpr size_t kNoAllocScratchBytes = 3u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on each device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress, once per device, with that device current.
+void* g_noalloc_ptr[64];
+int g_noalloc_status[64];
+std::once_flag g_noalloc_once[64];
+
+}  // namespace
+}  // namespace ngb
+
+extern "C" int ng_gemv_w4a16_noalloc(const void* x, int x_dtype, const int32_t* qweight,
+                                     const uint16_t* scales, void* y, int M, int K, int N,
+                                     int group_size, void* stream) {
+  using namespace ngb;
+  if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  const int d = dev.device;
+  std::call_once(g_noalloc_once[d], [d] {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_ptr[d] = p;
+    g_noalloc_status[d] = (e == cudaSuccess && p != nullptr) ? NG_OK : NG_ERR_CUDA;
+  });
+  if (g_noalloc_status[d] != NG_OK) return g_noalloc_status[d];
+  // The workspace this call needs must fit the fixed array.
+  const size_t need = gemv_tc_workspace_bytes(N, dev);
+  if (need > kNoAllocScratchBytes) return NG_ERR_BAD_SHAPE;
+  auto strm = static_cast<cudaStream_t>(stream);
+  // The arrival counters must start at zero.  A successful call leaves them at
+  // zero, but one that gave up on a bounded wait may not, so clear them on the
+  // stream first (a memset, not an allocation).
+  unsigned char* base = static_cast<unsigned char*>(g_noalloc_ptr[d]);
+  const size_t counters = tc_counter_offset(dev.sm_count);
+  if (cudaMemsetAsync(base + counters, 0, need - counters, strm) != cudaSuccess) return NG_ERR_CUDA;
+  return gemv_tc(x, x_dtype, reinterpret_cast<const uint32_t*>(qweight),
+                 reinterpret_cast<const __half*>(scales), y, M, K, N, group_size, base, dev, strm);
+}
