@@ -205,10 +205,11 @@ def run_step(args, wl, world, rank, local, dist):
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        t_end = time.perf_counter() + 0.5
-        while time.perf_counter() < t_end:
+        # A fixed replay count on every rank: each replay holds NCCL all-reduces,
+        # so all ranks must run the same number (a wall-clock loop would not).
+        for _ in range(300):
             graph.replay()
-            torch.cuda.synchronize()
+        torch.cuda.synchronize()
         if dist:
             dist.barrier()
         with torch.cuda.stream(stream):
