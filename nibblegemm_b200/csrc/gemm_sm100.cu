@@ -18,8 +18,9 @@
 //               to the stage's "empty" barrier; per tile, commit to "acc full"
 //   warp 2      tensor-memory allocator (2 x BT columns: double-buffered acc)
 //   warps 4-7   epilogue: tcgen05.ld 128 lanes x BT columns -> fp16/bf16 -> Y
-//   warps 8-15  dequant: two threads per weight column (n0 + t), each takes 4
-//               of the 8 packed rows of a k-step; it decodes them with the magic-number
+//   warps 8-15  dequant: two groups of four warps taking alternate k-steps (so
+//               each warp has two k-steps of time per stage); thread t owns
+//               weight column n0 + t and decodes the step's 8 packed rows with the magic-number
 //               method, applies the group scale (one rounding, so the fp16
 //               operand equals the reference's dequantised weight bit for
 //               bit), and writes one 128-byte row of the A tile in the
@@ -41,7 +42,8 @@ namespace {
 constexpr int kTileN = 128;        // weight columns per tile (MMA M)
 constexpr int kBK = 64;            // values of K per k-step (one 128-byte swizzle row)
 constexpr int kThreads = 512;
-constexpr int kDequantWarps = 8;  // warps 8..15: two threads per weight column
+constexpr int kDequantGroups = 2;  // warps 8..15: two groups of 4 warps, alternate k-steps
+constexpr int kDequantWarps = 4;   // warps per group (one thread per weight column)
 constexpr int kATileBytes = kTileN * kBK * 2;   // 16 KB decoded weights
 constexpr int kRawBytes = (kBK / 8) * kTileN * 4;  // 4 KB packed words
 constexpr int kSmemBudget = 220 * 1024;
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
     const int t = (threadIdx.x - 256) & (kTileN - 1);  // weight column within the tile
-    const int half = (threadIdx.x - 256) >> 7;           // which 4 of the 8 packed rows
+    const int grp = (threadIdx.x - 256) >> 7;            // this group decodes k-steps it % 2 == grp
     const int atom = t >> 3, r8 = t & 7;
     const int my_tiles = tiles > static_cast<int>(blockIdx.x)
                              ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
@@ -211,25 +213,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kPrefetch = 4;
     __half pf[kPrefetch];
 #pragma unroll
-    for (int j = 0; j < kPrefetch; ++j) pf[j] = scale_at(j);
-    for (int it = 0; it < total; ++it) {
+    for (int j = 0; j < kPrefetch; ++j) pf[j] = scale_at(grp + j * kDequantGroups);
+    for (int it = grp; it < total; it += kDequantGroups) {
       const int s = it % stages;
       const uint32_t ph = (it / stages) & 1;
       const __half sc = pf[0];
 #pragma unroll
       for (int j = 0; j + 1 < kPrefetch; ++j) pf[j] = pf[j + 1];
-      pf[kPrefetch - 1] = scale_at(it + kPrefetch);
+      pf[kPrefetch - 1] = scale_at(it + kPrefetch * kDequantGroups);
       if (!mbar_wait_bounded(&bars->full[s], ph, err, abort)) break;
       unsigned char* st = smem + s * kStageBytes;
       const uint32_t* raw = reinterpret_cast<const uint32_t*>(st + kATileBytes + kBTileBytes);
       unsigned char* arow = st + atom * 1024 + r8 * 128;
-      constexpr int kRowsPer = kBK / 16;  // 4 packed rows per thread
+      constexpr int kRowsPer = kBK / 8;  // all 8 packed rows of the k-step
       uint32_t qv[kRowsPer];
 #pragma unroll
-      for (int i = 0; i < kRowsPer; ++i) qv[i] = raw[(half * kRowsPer + i) * kTileN + t];
+      for (int i = 0; i < kRowsPer; ++i) qv[i] = raw[i * kTileN + t];
 #pragma unroll
       for (int i = 0; i < kRowsPer; ++i) {
-        const int r = half * kRowsPer + i;
+        const int r = i;
         const uint32_t q = qv[i];
         uint4 v;
         if constexpr (!BF16) {
