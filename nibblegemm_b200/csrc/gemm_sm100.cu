@@ -41,9 +41,13 @@ namespace {
 
 constexpr int kTileN = 128;        // weight columns per tile (MMA M)
 constexpr int kBK = 64;            // values of K per k-step (one 128-byte swizzle row)
-constexpr int kThreads = 512;
-constexpr int kDequantGroups = 2;  // warps 8..15: two groups of 4 warps, alternate k-steps
+#ifndef NG_GEMM_DQ_GROUPS
+#define NG_GEMM_DQ_GROUPS 2
+#endif
+// Dequant warps 8.. form kDequantGroups groups of 4 warps taking k-steps round-robin.
+constexpr int kDequantGroups = NG_GEMM_DQ_GROUPS;
 constexpr int kDequantWarps = 4;   // warps per group (one thread per weight column)
+constexpr int kThreads = 256 + kDequantGroups * kDequantWarps * 32;
 constexpr int kATileBytes = kTileN * kBK * 2;   // 16 KB decoded weights
 constexpr int kRawBytes = (kBK / 8) * kTileN * 4;  // 4 KB packed words
 constexpr int kSmemBudget = 220 * 1024;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
     const int t = (threadIdx.x - 256) & (kTileN - 1);  // weight column within the tile
-    const int grp = (threadIdx.x - 256) >> 7;            // this group decodes k-steps it % 2 == grp
+    const int grp = (threadIdx.x - 256) >> 7;            // this group decodes k-steps it % kDequantGroups == grp
     const int atom = t >> 3, r8 = t & 7;
     const int my_tiles = tiles > static_cast<int>(blockIdx.x)
                              ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
