@@ -179,7 +179,7 @@ def run_reference(args, rank):
 
 
 def run_step(args, wl, world, rank, local, dist):
-    """Tokens/s of the Llama-3-8B INT4 projection stack (SURVEY row a15 / 8e).
+    """Tokens/s of the Llama-3-8B INT4 projection stack.
 
     One step = one batch-1 token through all 224 decoder projections; under
     torchrun the projections are Megatron-sharded over the ranks with an NCCL
@@ -188,7 +188,7 @@ def run_step(args, wl, world, rank, local, dist):
     """
     import nibblegemm_b200 as ng
     from nibblegemm_b200.decode_step import LLAMA3_8B, ProjectionStackStep
-    step = ProjectionStackStep(LLAMA3_8B, batch=1, rank=rank, world=world)
+    step = ProjectionStackStep(LLAMA3_8B, batch=1, rank=rank, world=world, reduce=args.reduce)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -255,14 +255,15 @@ def run_step(args, wl, world, rank, local, dist):
             "data": "synthetic random-init INT4 weights (BASELINE distributions), batch-1 activations",
             "config": {"workload": wl["name"], "layers": 32, "hidden": 4096, "kv": 1024,
                        "intermediate": 14336, "group_size": 128, "batch": 1,
-                       "parallelism": f"tp{world}", "l2": "3.6 GB of distinct weights per token (>> L2)",
+                       "parallelism": f"tp{world}",
+                       "tp_reduce": (args.reduce if world > 1 else None), "l2": "3.6 GB of distinct weights per token (>> L2)",
                        "timing": "one CUDA graph per token, replayed `steps` times"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": None,
                          "peak_source": f"{src} copy bandwidth", "algorithmic_bytes_per_step_per_rank": wbytes},
             "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8192,
                     "d2h_bytes_per_step": 8192, "path": "ProjectionStackStep.step() eager"},
-            "gpu_launches": 224,
+            "gpu_launches": 224 + (64 if (world > 1 and args.reduce == "peer") else 0),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -278,6 +279,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gemv")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
+                    help="tensor-parallel all-reduce of the step8b workload")
     ap.add_argument("--algo", type=int, default=0, help="GEMV schedule (see ng_gemv_w4a16)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: run the op warmup+1 times eagerly on one GPU and exit")

@@ -150,6 +150,29 @@ int ng_gemv_w4a16_noalloc(const void* x, int x_dtype, const int32_t* qweight,
 int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
                   void* y, int M, int K, int N, int group_size, int tile_tokens, void* stream);
 
+/*
+ * Tensor-parallel reduction for the decode step: one-shot all-reduce (sum) of
+ * a small fp16/bf16 vector across the `world` GPUs of one node over NVLink
+ * peer memory.  No counterpart in the reference (single-GPU); replaces the
+ * NCCL all-reduce after each row-parallel projection.
+ *   Set-up (once per communicator): every rank allocates a zero-filled device
+ *   buffer of ng_allreduce_buffer_bytes(world, max_elems) bytes and a
+ *   zero-filled array of 16 uint32 call counters (`epochs`), exports the
+ *   buffer with cudaIpcGetMemHandle, and maps the peers' buffers with
+ *   ng_ipc_open.  `peer_buffers[p]` is rank p's buffer as mapped in this
+ *   process (this rank's own buffer at index `rank`).
+ *   Each call: every rank calls with the same n (<= max_elems) in the same
+ *   order; `data` is reduced in place; the sum is taken in fp32 in rank order
+ *   (every rank gets bit-identical results).  The kernel waits (bounded) for
+ *   the peers' arrivals; a timeout is reported by ng_device_status.
+ */
+size_t ng_allreduce_buffer_bytes(int world, size_t max_elems);
+int ng_allreduce_sum(void* data, int dtype, size_t n, void* const* peer_buffers, int rank,
+                     int world, size_t max_elems, unsigned int* epochs, void* stream);
+/* Map a peer's exported buffer (64-byte cudaIpcMemHandle) / unmap it. */
+int ng_ipc_open(const void* handle, void** dev_ptr);
+int ng_ipc_close(void* dev_ptr);
+
 #ifdef __cplusplus
 }
 #endif

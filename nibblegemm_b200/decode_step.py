@@ -88,8 +88,12 @@ class ProjectionStackStep:
 
     def __init__(self, cfg=LLAMA3_8B, batch: int = 1, group_size: int = 128, rank: int = 0,
                  world: int = 1, device: Optional[torch.device] = None, seed: int = 0,
-                 dtype: torch.dtype = torch.float16, layers: Optional[int] = None):
+                 dtype: torch.dtype = torch.float16, layers: Optional[int] = None,
+                 reduce: str = "peer"):
+        if reduce not in ("peer", "nccl"):
+            raise ValueError(f"reduce must be 'peer' or 'nccl', not {reduce!r}")
         self.cfg, self.batch, self.rank, self.world = cfg, batch, rank, world
+        self.reduce = reduce
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
         self.ext = extension()
@@ -117,6 +121,13 @@ class ProjectionStackStep:
                 layer.append(Projection(name, style, w, x,
                                         torch.empty(batch, w.N, dtype=dtype, device=self.device)))
             self.proj.append(layer)
+        # Row-parallel outputs are summed across ranks: by default with the
+        # one-shot peer-memory all-reduce (ng_allreduce_sum), else NCCL.
+        self._peer = None
+        if world > 1 and reduce == "peer":
+            from .comm import PeerAllReduce
+            max_n = max(p.y.numel() for layer in self.proj for p in layer if p.style == "row")
+            self._peer = PeerAllReduce(max_n, device=self.device)
 
     @property
     def weight_bytes(self) -> int:
@@ -133,4 +144,7 @@ class ProjectionStackStep:
                 else:
                     ext.gemm_w4a16(p.x, p.weight.qweight, p.weight.scales, p.weight.group_size, out=p.y)
                 if p.style == "row" and self.world > 1:
-                    torch.distributed.all_reduce(p.y)
+                    if self._peer is not None:
+                        self._peer(p.y)
+                    else:
+                        torch.distributed.all_reduce(p.y)

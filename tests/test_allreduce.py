@@ -1,0 +1,131 @@
+"""The tensor-parallel reduction (``ng_allreduce_sum`` / ``PeerAllReduce``).
+
+CPU: the buffer-size arithmetic and argument validation (no launch).
+GPU (two devices): the one-shot peer-memory sum against an fp32 sum in rank
+order rounded once -- bit-exact, since the kernel computes exactly that --
+over message sizes that exercise the vector and scalar copy paths and the
+CTA split, repeated calls (both slot parities), and CUDA-graph replay.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from nibblegemm_b200 import _lib
+
+FAKE = 1 << 20
+
+
+def _codes():
+    from tests.test_capi import status_codes
+    return status_codes()
+
+
+def test_buffer_bytes():
+    lib = _lib.load()
+    # 2 parities x 16 CTAs x world slots of ceil(n/16) rounded to 8 elems, 2 B each,
+    # then 2 x 16 x 8 uint32 flags.
+    for world, n in [(2, 4096), (8, 4096), (4, 1), (2, 14336 * 4)]:
+        slot = ((n + 15) // 16 + 7) // 8 * 8
+        assert lib.ng_allreduce_buffer_bytes(world, n) == 2 * 16 * world * slot * 2 + 2 * 16 * 8 * 4
+    assert lib.ng_allreduce_buffer_bytes(0, 4096) == 0
+    assert lib.ng_allreduce_buffer_bytes(9, 4096) == 0
+
+
+def test_argument_validation():
+    lib = _lib.load()
+    c = _codes()
+    ptrs = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    assert lib.ng_allreduce_sum(None, 0, 16, ptrs, 0, 2, 64, FAKE, None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_allreduce_sum(FAKE, 0, 16, None, 0, 2, 64, FAKE, None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_allreduce_sum(FAKE, 0, 16, ptrs, 0, 2, 64, None, None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_allreduce_sum(FAKE, 5, 16, ptrs, 0, 2, 64, FAKE, None) == c["NG_ERR_BAD_DTYPE"]
+    assert lib.ng_allreduce_sum(FAKE, 0, 16, ptrs, 2, 2, 64, FAKE, None) == c["NG_ERR_BAD_ARGUMENT"]
+    assert lib.ng_allreduce_sum(FAKE, 0, 16, ptrs, 0, 9, 64, FAKE, None) == c["NG_ERR_BAD_ARGUMENT"]
+    assert lib.ng_allreduce_sum(FAKE, 0, 0, ptrs, 0, 2, 64, FAKE, None) == c["NG_ERR_BAD_SHAPE"]
+    assert lib.ng_allreduce_sum(FAKE, 0, 65, ptrs, 0, 2, 64, FAKE, None) == c["NG_ERR_BAD_SHAPE"]
+    assert lib.ng_allreduce_sum(FAKE + 1, 0, 16, ptrs, 0, 2, 64, FAKE, None) == c["NG_ERR_MISALIGNED"]
+    assert lib.ng_ipc_open(None, None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_ipc_close(None) == c["NG_ERR_NULL_POINTER"]
+
+
+def _rank_input(n, dtype, rank, call):
+    g = torch.Generator().manual_seed(1000 * call + 7 * rank + n)
+    return torch.randn(n, generator=g).to(dtype)
+
+
+def _expected(n, dtype, world, call):
+    acc = torch.zeros(n, dtype=torch.float32)
+    for r in range(world):
+        acc += _rank_input(n, dtype, r, call).float()
+    return acc.to(dtype)
+
+
+SIZES = [4096, 14336, 1, 8, 333, 4096 * 16 + 24]
+MAX_N = max(SIZES)
+
+
+def _ar_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from nibblegemm_b200.comm import PeerAllReduce
+    from nibblegemm_b200 import ops
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    fails = []
+    try:
+        ar = PeerAllReduce(MAX_N)
+        call = 0
+        for dtype in (torch.float16, torch.bfloat16):
+            for n in SIZES:
+                for _ in range(3):  # both parities, then the first again
+                    t = _rank_input(n, dtype, rank, call).cuda()
+                    ar(t)
+                    if not torch.equal(t.cpu(), _expected(n, dtype, world, call)):
+                        fails.append((str(dtype), n, call))
+                    call += 1
+        # graph replay: inputs refreshed in place between replays
+        n = 14336
+        buf = torch.empty(n, dtype=torch.float16, device="cuda")
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                ar(buf)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(4):
+            buf.copy_(_rank_input(n, torch.float16, rank, call).cuda())
+            g.replay()
+            if not torch.equal(buf.cpu(), _expected(n, torch.float16, world, call)):
+                fails.append(("graph", n, call))
+            call += 1
+        torch.cuda.synchronize()
+        status = ops.extension().device_status()
+        q.put((rank, fails, status))
+        dist.barrier()
+        ar.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_allreduce_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ar_worker, args=(r, 2, 29723, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, fails, status in results:
+        assert not fails, (rank, fails[:5])
+        assert status == 0, (rank, status)

@@ -51,13 +51,13 @@ def test_tp1_projections_match_oracle_and_graph_replay():
         assert torch.equal(a, p.y), p.name
 
 
-def _tp_worker(rank, world, port, q):
+def _tp_worker(rank, world, port, q, reduce):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        step = ProjectionStackStep(LLAMA3_8B, batch=2, layers=1, rank=rank, world=world)
+        step = ProjectionStackStep(LLAMA3_8B, batch=2, layers=1, rank=rank, world=world, reduce=reduce)
         step.step()
         torch.cuda.synchronize()
         outs = {}
@@ -80,10 +80,11 @@ def _tp_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_matches_tp1():
+@pytest.mark.parametrize("reduce,port", [("peer", 29711), ("nccl", 29713)])
+def test_tp2_matches_tp1(reduce, port):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, 29711, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, reduce)) for r in range(2)]
     for p in procs:
         p.start()
     errs = q.get(timeout=300)
