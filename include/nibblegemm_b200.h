@@ -155,11 +155,11 @@ int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint
  * a small fp16/bf16 vector across the `world` GPUs of one node over NVLink
  * peer memory.  No counterpart in the reference (single-GPU); replaces the
  * NCCL all-reduce after each row-parallel projection.
- *   Set-up (once per communicator): every rank allocates a zero-filled device
- *   buffer of ng_allreduce_buffer_bytes(world, max_elems) bytes and a
- *   zero-filled array of 16 uint32 call counters (`epochs`), exports the
- *   buffer with cudaIpcGetMemHandle, and maps the peers' buffers with
- *   ng_ipc_open.  `peer_buffers[p]` is rank p's buffer as mapped in this
+ *   Set-up (once per communicator): every rank allocates its exchange buffer
+ *   of ng_allreduce_buffer_bytes(world, max_elems) bytes with ng_ipc_alloc
+ *   (zero-filled, exported as a 64-byte CUDA IPC handle) and a zero-filled
+ *   array of 16 uint32 call counters (`epochs`), passes the handle to its
+ *   peers, and maps the peers' buffers with ng_ipc_open.  `peer_buffers[p]` is rank p's buffer as mapped in this
  *   process (this rank's own buffer at index `rank`).
  *   Each call: every rank calls with the same n (<= max_elems) in the same
  *   order; `data` is reduced in place; the sum is taken in fp32 in rank order
@@ -169,7 +169,11 @@ int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint
 size_t ng_allreduce_buffer_bytes(int world, size_t max_elems);
 int ng_allreduce_sum(void* data, int dtype, size_t n, void* const* peer_buffers, int rank,
                      int world, size_t max_elems, unsigned int* epochs, void* stream);
-/* Map a peer's exported buffer (64-byte cudaIpcMemHandle) / unmap it. */
+/* Allocate a zero-filled buffer on the current device and write its 64-byte
+ * IPC handle to `handle` / free it.  Map a peer's buffer from its handle /
+ * unmap it. */
+int ng_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+int ng_ipc_free(void* dev_ptr);
 int ng_ipc_open(const void* handle, void** dev_ptr);
 int ng_ipc_close(void* dev_ptr);
 

@@ -29,6 +29,8 @@ SIGNATURES = {
     "ng_gemv_w4a16_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ng_allreduce_buffer_bytes": (ctypes.c_size_t, [_I, ctypes.c_size_t]),
     "ng_allreduce_sum": (_I, [_P, _I, ctypes.c_size_t, _P, _I, _I, ctypes.c_size_t, _P, _P]),
+    "ng_ipc_alloc": (_I, [ctypes.c_size_t, _P, _P]),
+    "ng_ipc_free": (_I, [_P]),
     "ng_ipc_open": (_I, [_P, _P]),
     "ng_ipc_close": (_I, [_P]),
     "ng_gemm_w4a16": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),

@@ -30,24 +30,27 @@ class PeerAllReduce:
         nbytes = self.lib.ng_allreduce_buffer_bytes(self.world, self.max_elems)
         if nbytes == 0:
             raise RuntimeError(f"unsupported world size {self.world}")
-        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         self.epochs = torch.zeros(16, dtype=torch.int32, device=self.device)
-        torch.cuda.synchronize(self.device)
-        meta = self.buf.untyped_storage()._share_cuda_()
-        handle, offset = bytes(meta[1]), int(meta[3])
+        # The exchange buffer is the library's own cudaMalloc (not the torch
+        # caching allocator), so its IPC handle covers exactly this buffer.
+        with torch.cuda.device(self.device):
+            base, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+            _lib.check(self.lib.ng_ipc_alloc(nbytes, ctypes.byref(base), handle), "ng_ipc_alloc")
+        self._base = base.value
         infos = [None] * self.world
-        dist.all_gather_object(infos, (handle, offset), group=group)
+        dist.all_gather_object(infos, handle.raw, group=group)
         self._opened = []
         ptrs = []
-        for p, (h, off) in enumerate(infos):
+        for p, h in enumerate(infos):
             if p == self.rank:
-                ptrs.append(self.buf.data_ptr())
+                ptrs.append(self._base)
                 continue
-            hb = ctypes.create_string_buffer(h, len(h))
             out = ctypes.c_void_p()
-            _lib.check(self.lib.ng_ipc_open(hb, ctypes.byref(out)), "ng_ipc_open")
+            with torch.cuda.device(self.device):
+                _lib.check(self.lib.ng_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(out)),
+                           "ng_ipc_open")
             self._opened.append(out.value)
-            ptrs.append(out.value + off)
+            ptrs.append(out.value)
         self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         dist.barrier(group=group)
 
@@ -61,6 +64,11 @@ class PeerAllReduce:
         return t
 
     def close(self):
+        """Unmap the peers' buffers, then free this rank's (call on every rank,
+        after a barrier, when no reduction is in flight)."""
         for p in self._opened:
             self.lib.ng_ipc_close(p)
         self._opened = []
+        if self._base:
+            self.lib.ng_ipc_free(self._base)
+            self._base = None

@@ -156,6 +156,27 @@ extern "C" int ng_allreduce_sum(void* data, int dtype, size_t n, void* const* pe
   return launch_status();
 }
 
+extern "C" int ng_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+  if (!dev_ptr || !handle) return NG_ERR_NULL_POINTER;
+  if (bytes == 0) return NG_ERR_BAD_SHAPE;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return NG_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return NG_ERR_CUDA;
+  }
+  memcpy(handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return NG_OK;
+}
+
+extern "C" int ng_ipc_free(void* dev_ptr) {
+  if (!dev_ptr) return NG_ERR_NULL_POINTER;
+  return cudaFree(dev_ptr) == cudaSuccess ? NG_OK : NG_ERR_CUDA;
+}
+
 extern "C" int ng_ipc_open(const void* handle, void** dev_ptr) {
   if (!handle || !dev_ptr) return NG_ERR_NULL_POINTER;
   cudaIpcMemHandle_t h;

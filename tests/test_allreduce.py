@@ -52,6 +52,8 @@ def test_argument_validation():
     assert lib.ng_allreduce_sum(FAKE + 1, 0, 16, ptrs, 0, 2, 64, FAKE, None) == c["NG_ERR_MISALIGNED"]
     assert lib.ng_ipc_open(None, None) == c["NG_ERR_NULL_POINTER"]
     assert lib.ng_ipc_close(None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_ipc_free(None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_ipc_alloc(64, None, None) == c["NG_ERR_NULL_POINTER"]
 
 
 def _rank_input(n, dtype, rank, call):
@@ -110,6 +112,9 @@ def _ar_worker(rank, world, port, q):
         q.put((rank, fails, status))
         dist.barrier()
         ar.close()
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, [repr(e)], -1))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -122,7 +127,7 @@ def test_peer_allreduce_two_gpus():
     procs = [ctx.Process(target=_ar_worker, args=(r, 2, 29723, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=240) for _ in procs]
+    results = [q.get(timeout=150) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

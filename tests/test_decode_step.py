@@ -75,6 +75,9 @@ def _tp_worker(rank, world, port, q, reduce):
             errs = {p.name: float((outs[p.name] - p.y.float().cpu()).abs().max() / p.y.float().cpu().abs().max())
                     for p in ref.proj[0]}
             q.put(errs)
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put({"worker error": repr(e)})
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -87,9 +90,10 @@ def test_tp2_matches_tp1(reduce, port):
     procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, reduce)) for r in range(2)]
     for p in procs:
         p.start()
-    errs = q.get(timeout=300)
+    errs = q.get(timeout=150)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    assert "worker error" not in errs, errs
     for name, e in errs.items():
         assert e <= 5e-3, (name, e)
