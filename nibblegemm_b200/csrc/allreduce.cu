@@ -4,8 +4,8 @@
 // batch 1).  At these sizes the cost is latency, not bandwidth: NCCL's ring
 // takes ~2(world-1) dependent hops; here every rank pushes its vector straight
 // into a slot of every peer's buffer (plain P2P stores, one NVLink crossing),
-// raises a flag there, waits for the world's flags in its own memory, and sums
-// the slots in rank order -- so every rank computes the identical, deterministic
+// raises a flag there, waits for the peers' flags in its own memory, and sums
+// its own vector and the peers' slots in rank order -- so every rank computes the identical, deterministic
 // result in fp32 and rounds once.
 //
 // Buffer of each rank (mapped into every peer with CUDA IPC):
@@ -48,6 +48,11 @@ __global__ void __launch_bounds__(kArThreads)
     allreduce_kernel(unsigned short* __restrict__ io, long long n, PeerPtrs peers, int rank,
                      int world, long long slot_elems, unsigned int* __restrict__ epochs,
                      unsigned int* __restrict__ err) {
+  // Launched with programmatic stream serialisation: let the next kernel (the
+  // next projection's GEMV, which prefetches weights before its own
+  // griddepcontrol.wait) launch now, and wait for the producer of `io`.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int c = blockIdx.x;
   const long long per = (n + gridDim.x - 1) / gridDim.x;
   const long long e0 = c * per, e1 = e0 + per < n ? e0 + per : n;
@@ -66,10 +71,12 @@ __global__ void __launch_bounds__(kArThreads)
     return f + (static_cast<size_t>(par) * kMaxCtas + c) * kMaxWorld + src;
   };
 
-  // 1. push this rank's chunk into slot `rank` of every rank's buffer
+  // 1. push this rank's chunk into slot `rank` of every peer's buffer (our
+  //    own contribution is read straight from `io` in step 4)
+  const unsigned short* src = io + e0;
   for (int p = 0; p < world; ++p) {
+    if (p == rank) continue;
     unsigned short* dst = slot(peers.data[p], rank);
-    const unsigned short* src = io + e0;
     if ((cnt & 7) == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
       for (long long i = threadIdx.x; i < cnt / 8; i += kArThreads)
         reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
@@ -77,12 +84,14 @@ __global__ void __launch_bounds__(kArThreads)
       for (long long i = threadIdx.x; i < cnt; i += kArThreads) dst[i] = src[i];
     }
   }
-  __threadfence_system();
+  // 2. raise our flag in every peer's buffer.  The CTA barrier orders every
+  //    thread's pushes before the flag writers' system-scope release stores
+  //    (release is cumulative over what the barrier made visible to them).
   __syncthreads();
-  // 2. raise our flag in every rank's buffer
-  if (threadIdx.x < world) st_release_sys(flag(peers.data[threadIdx.x], rank), epoch + 1);
-  // 3. wait (bounded) for every rank's flag in our own buffer
-  if (threadIdx.x < world) {
+  if (threadIdx.x < world && threadIdx.x != rank)
+    st_release_sys(flag(peers.data[threadIdx.x], rank), epoch + 1);
+  // 3. wait (bounded) for every peer's flag in our own buffer
+  if (threadIdx.x < world && threadIdx.x != rank) {
     const unsigned int* f = flag(peers.data[rank], threadIdx.x);
     const uint64_t t0 = global_timer_ns();
     while (ld_acquire_sys(f) != epoch + 1) {
@@ -93,11 +102,12 @@ __global__ void __launch_bounds__(kArThreads)
     }
   }
   __syncthreads();
-  // 4. sum the world's slots in rank order (identical on every rank)
+  // 4. sum the world's contributions in rank order (identical on every rank)
+  const unsigned short* mine = slot(peers.data[rank], 0);
   for (long long i = threadIdx.x; i < cnt; i += kArThreads) {
     float acc = 0.f;
     for (int s = 0; s < world; ++s) {
-      const unsigned short v = slot(peers.data[rank], s)[i];
+      const unsigned short v = s == rank ? src[i] : mine[s * slot_elems + i];
       acc += BF16 ? __uint_as_float(static_cast<uint32_t>(v) << 16) : __half2float(__ushort_as_half(v));
     }
     io[e0 + i] = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(acc)) : __half_as_ushort(__float2half_rn(acc));
@@ -145,15 +155,22 @@ extern "C" int ng_allreduce_sum(void* data, int dtype, size_t n, void* const* pe
   ctas = ctas < 1 ? 1 : (ctas > kMaxCtas ? kMaxCtas : ctas);
   while ((static_cast<long long>(n) + ctas - 1) / ctas > slot) ++ctas;
   if (ctas > kMaxCtas) return NG_ERR_BAD_SHAPE;
-  auto strm = static_cast<cudaStream_t>(stream);
   auto* io = static_cast<unsigned short*>(data);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas, 1, 1);
+  cfg.blockDim = dim3(kArThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const long long nn = static_cast<long long>(n);
   if (dtype == NG_DTYPE_BF16)
-    allreduce_kernel<true><<<ctas, kArThreads, 0, strm>>>(io, static_cast<long long>(n), peers, rank,
-                                                          world, slot, epochs, dev.err);
-  else
-    allreduce_kernel<false><<<ctas, kArThreads, 0, strm>>>(io, static_cast<long long>(n), peers, rank,
-                                                           world, slot, epochs, dev.err);
-  return launch_status();
+    return launch_status(cudaLaunchKernelEx(&cfg, allreduce_kernel<true>, io, nn, peers, rank, world,
+                                            slot, epochs, dev.err));
+  return launch_status(cudaLaunchKernelEx(&cfg, allreduce_kernel<false>, io, nn, peers, rank, world,
+                                          slot, epochs, dev.err));
 }
 
 extern "C" int ng_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
