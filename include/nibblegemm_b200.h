@@ -98,7 +98,12 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
  *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x);
  *     algo 0 = 1 for fp16 x, 2 for bf16 x.
- *   Both are launched with programmatic stream serialisation: they start
+ *   - bulk-copy ring (algo 4; M <= 8; the workspace is not used): one producer
+ *     warp per CTA streams the CTA's (128-column, K-slice) weight block into a
+ *     shared-memory ring with cp.async.bulk, consumer warps decode from shared
+ *     memory with the algo 1 (fp16 x) / algo 2 (bf16 x) arithmetic; `splits`
+ *     1..8 or 0 = heuristic, K slices reduced in a cluster as above.
+ *   All are launched with programmatic stream serialisation: they start
  *   streaming their read-only weights while the previous kernel on the stream
  *   finishes, and read x / write y / touch the workspace only after it has.
  *   x, qweight 16-byte aligned; scales 8-byte aligned.

@@ -394,7 +394,8 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
   if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
   if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
-  if (algo < 0 || algo > 3) return NG_ERR_BAD_ARGUMENT;
+  if (algo < 0 || algo > 4) return NG_ERR_BAD_ARGUMENT;
+  if (algo == 4 && (M > 8 || splits > 8)) return NG_ERR_BAD_ARGUMENT;
   if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
   if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2) ||
       !aligned(workspace, 256))
@@ -413,6 +414,8 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
       return gemv_tc(x, x_dtype, q, s, y, M, K, N, group_size, workspace, dev, strm);
     }
   }
+  if (algo == 4)
+    return gemv_ring(x, x_dtype, false, q, s, y, M, K, N, group_size, splits, dev, strm);
   const int threads = block_threads ? block_threads : 256;
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_w<true, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);

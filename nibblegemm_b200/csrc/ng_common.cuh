@@ -133,6 +133,11 @@ int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void
             int N, int G, void* ws, const DeviceInfo& dev, cudaStream_t strm);
 
 
+// Bulk-copy ring GEMV (gemv_ring.cu), M <= 8; arguments already validated.
+int gemv_ring(const void* x, int x_dtype, bool float_path, const uint32_t* q, const __half* s,
+              void* y, int M, int K, int N, int G, int splits, const DeviceInfo& dev,
+              cudaStream_t strm);
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }
