@@ -90,19 +90,22 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     depend on M or N and each call leaves the part that must start at zero
  *     (per-tile arrival counters) at zero.  Calls sharing a workspace must not
  *     overlap on the GPU (one workspace per stream).
- *   - CUDA-core cluster split-K (default, algo 0 / 1 / 2; the workspace is
+ *   - CUDA-core cluster split-K (algo 1 / 2; the workspace is
  *     not used): `splits` K slices (1..16, 0 = heuristic,
  *     raised if needed so a slice's activations fit on chip) reduced through
  *     distributed shared memory inside a thread-block cluster, fixed rank
  *     order; block_threads 0 (256), 128 or 256;  algo 1 = fp16 decode with
  *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
- *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x);
- *     algo 0 = 1 for fp16 x, 2 for bf16 x.
- *   - bulk-copy ring (algo 4; M <= 8; the workspace is not used): one producer
- *     warp per CTA streams the CTA's (128-column, K-slice) weight block into a
- *     shared-memory ring with cp.async.bulk, consumer warps decode from shared
- *     memory with the algo 1 (fp16 x) / algo 2 (bf16 x) arithmetic; `splits`
- *     1..8 or 0 = heuristic, K slices reduced in a cluster as above.
+ *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x).
+ *   - algo 0 (default): algo 5 below when M <= 8 and either the packed weight
+ *     is >= 12 MiB or M > 4; otherwise algo 1 (fp16 x) / algo 2 (bf16 x).
+ *   - bulk-copy ring (algo 4 / 5; M <= 8; the workspace is not used): one
+ *     producer warp per CTA streams the CTA's (128-column, K-slice) weight
+ *     block into a shared-memory ring with cp.async.bulk, consumer warps
+ *     decode from shared memory -- algo 4 with the algo 1 (fp16 x) / algo 2
+ *     (bf16 x) arithmetic, algo 5 on the tensor pipe (magic-number operands to
+ *     mma.sync, fp32 accumulation, offsets removed by a correction MMA);
+ *     `splits` 1..8 or 0 = heuristic, K slices reduced in a cluster as above.
  *   All are launched with programmatic stream serialisation: they start
  *   streaming their read-only weights while the previous kernel on the stream
  *   finishes, and read x / write y / touch the workspace only after it has.

@@ -6,8 +6,8 @@
 // flight as it has warps x registers; with few chunks per warp the load
 // latency, the activation staging and the reductions are paid in series.
 // Here one producer warp per CTA streams the CTA's whole weight slice with
-// `cp.async.bulk` (one 512-byte row segment per lane, completion counted on
-// an mbarrier) into a ring of 16 KB stages, and it starts doing so *before*
+// 2-D TMA loads (4 KB boxes of 128 columns x 8 packed rows, completion counted
+// on an mbarrier) into a ring of stages, and it starts doing so *before*
 // `griddepcontrol.wait`: weights are read-only, so under programmatic
 // dependent launch the slice is already in flight while the previous kernel
 // on the stream drains.  With one CTA per SM the ring holds most or all of
@@ -33,8 +33,11 @@
 //     kErrWaitTimeout, stops, waits (bounded) for the copies it issued, and
 //     returns through the normal reduction path.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -47,13 +50,15 @@ namespace ngb {
 namespace {
 
 constexpr int kRCols = 128;                       // columns per tile
-constexpr int kRowsPerWarp = 4;                   // packed rows per consumer warp per stage
 constexpr int kMaxRingCluster = 8;
 
-enum RPath { kRHalf2 = 0, kRFloat2 = 1 };
+// Consumer arithmetic: CUDA-core half2 / fp32x2 (4 packed rows per warp per
+// stage), or mma.sync on magic-number operands (16 rows per warp per stage).
+enum RPath { kRHalf2 = 0, kRFloat2 = 1, kRMma = 2 };
 
-template <int CW>
+template <int CW, int PATH, int RW>
 struct RingCfg {
+  static constexpr int kRowsPerWarp = RW;
   static constexpr int kStageRows = CW * kRowsPerWarp;
   static constexpr int kStageBytes = kStageRows * kRCols * 4;
   static constexpr int kThreads = (CW + 1) * 32;  // + one producer warp
@@ -79,12 +84,16 @@ struct RingLayout {
   }
 };
 
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                         uint64_t policy) {
+constexpr int kBoxRows = 8;  // packed rows per TMA box: 128 x 8 words = 4 KB
+
+// 2-D tiled TMA load of one (128-column, 8-row) box of the packed weight,
+// L2 evict-first (each weight byte is read once).  No multicast.
+__device__ __forceinline__ void tma_box_g2s(void* dst, const CUtensorMap* map, uint64_t* bar, int col,
+                                            int row, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(col), "r"(row), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 
@@ -103,12 +112,58 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
-template <int MT, bool XBF16, int PATH, int CW>
-__global__ void __launch_bounds__(RingCfg<CW>::kThreads, 1)
-    gemv_ring_kernel(const void* __restrict__ x, const uint32_t* __restrict__ qw,
+template <bool BF16>
+__device__ __forceinline__ void ring_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// Magic-number MMA operands of one packed word, no subtract: h[p] holds the
+// code pair p (k = 2p, 2p + 1) as two 16-bit values.
+//   fp16: pairs 0 and 2 as 1024 + u; pairs 1 and 3 as 1024 + 16u, read in
+//         place from nibble bits 4..7 of each half (one AND/OR, no shift) --
+//         the matching activations are staged pre-divided by 16, so the
+//         product is (64 + u) * x.  1 shift + 4 AND/OR per word.
+//   bf16: every pair as 128 + u (bit 7 of a bf16 is exponent, so the high
+//         nibbles are shifted down).  3 shifts + 4 AND/OR per word.
+// Either way the product with x is exact in the fp32 accumulator; the offsets
+// (fp16: 1032 x on pairs 0/2, 72 * 16 (x/16) on pairs 1/3; bf16: 136 x) are
+// removed by a correction MMA with those constants as the A operand.
+template <bool BF16>
+__device__ __forceinline__ void decode_mma_operands(uint32_t q, uint32_t (&h)[4]) {
+  if constexpr (BF16) {
+    h[0] = and_or(q, 0x000F000Fu, 0x43004300u);
+    h[1] = and_or(q >> 4, 0x000F000Fu, 0x43004300u);
+    h[2] = and_or(q >> 8, 0x000F000Fu, 0x43004300u);
+    h[3] = and_or(q >> 12, 0x000F000Fu, 0x43004300u);
+  } else {
+    const uint32_t q8 = q >> 8;
+    h[0] = and_or(q, 0x000F000Fu, 0x64006400u);
+    h[1] = and_or(q, 0x00F000F0u, 0x64006400u);
+    h[2] = and_or(q8, 0x000F000Fu, 0x64006400u);
+    h[3] = and_or(q8, 0x00F000F0u, 0x64006400u);
+  }
+}
+
+template <int MT, bool XBF16, int PATH, int CW, int RW>
+__global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
+    gemv_ring_kernel(const __grid_constant__ CUtensorMap tmap_q, const void* __restrict__ x,
                      const __half* __restrict__ scales, void* __restrict__ y, int M, int K, int N,
                      int G, int rows_per_cta, int csize, int stages, unsigned int* __restrict__ err) {
-  using Cfg = RingCfg<CW>;
+  using Cfg = RingCfg<CW, PATH, RW>;
+  constexpr int kRowsPerWarp = Cfg::kRowsPerWarp;
   using XS = typename std::conditional<PATH == kRFloat2, float, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -154,8 +209,6 @@ __global__ void __launch_bounds__(RingCfg<CW>::kThreads, 1)
 
   if (warp == CW) {
     // ---------------- producer: stream the slice through the ring ----------------
-    const int ncols = min(kRCols, N - c0);
-    const uint32_t row_bytes = static_cast<uint32_t>(ncols) * 4u;
     const uint64_t pol = make_evict_first_policy();
     int issued = 0;
     for (int s = 0; s < nst; ++s) {
@@ -166,14 +219,13 @@ __global__ void __launch_bounds__(RingCfg<CW>::kThreads, 1)
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       }
       const int rows_here = min(Cfg::kStageRows, nrows - s * Cfg::kStageRows);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], rows_here * row_bytes);
+      const int boxes = rows_here / kBoxRows;  // slices are whole multiples of 8 rows
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], boxes * (kBoxRows * kRCols * 4));
       __syncwarp();
       unsigned char* dst = ring + static_cast<size_t>(slot) * Cfg::kStageBytes;
-      for (int r = lane; r < rows_here; r += 32) {
-        const int grow = kr0 + s * Cfg::kStageRows + r;
-        bulk_g2s(dst + r * (kRCols * 4), qw + static_cast<size_t>(grow) * N + c0, row_bytes,
-                 &full[slot], pol);
-      }
+      for (int b = lane; b < boxes; b += 32)
+        tma_box_g2s(dst + b * (kBoxRows * kRCols * 4), &tmap_q, &full[slot], c0,
+                    kr0 + s * Cfg::kStageRows + b * kBoxRows, pol);
       issued = s + 1;
     }
     // Drain: every copy this CTA issued has landed before shared memory is
@@ -215,6 +267,12 @@ __global__ void __launch_bounds__(RingCfg<CW>::kThreads, 1)
         }
         reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
         reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+      } else if constexpr (PATH == kRMma && !XBF16) {
+        // pairs 1 and 3 (k = 2,3 and 6,7 of the row) meet the 16u operands
+        const __half2 sixteenth = __float2half2_rn(0.0625f);
+        v.y = h2_bits(__hmul2(h2_from_bits(v.y), sixteenth));
+        v.w = h2_bits(__hmul2(h2_from_bits(v.w), sixteenth));
+        *reinterpret_cast<uint4*>(dst) = v;
       } else {
         *reinterpret_cast<uint4*>(dst) = v;
       }
@@ -222,103 +280,201 @@ __global__ void __launch_bounds__(RingCfg<CW>::kThreads, 1)
     asm volatile("cp.async.wait_all;" ::: "memory");
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");  // consumers only
 
-    for (int s = 0; s < nst; ++s) {
-      const int slot = s % stages;
-      if (!mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) break;
-      const int rows_here = min(Cfg::kStageRows, nrows - s * Cfg::kStageRows);
-      const int rr0 = warp * kRowsPerWarp;
-      if (rr0 < rows_here) {
-        const unsigned char* src = ring + static_cast<size_t>(slot) * Cfg::kStageBytes;
-        uint4 q[kRowsPerWarp];
+    if constexpr (PATH == kRMma) {
+      // Fragment mapping (m16n8k16; lane = 4g + t).  Per 4-row step the lane
+      // holds packed row (step + t), 16-byte runs at columns 64h + 4g and
+      // 64h + 32 + 4g (h = 0, 1):  A row g <-> column 64h + 4g + i and A row
+      // g + 8 <-> column 64h + 32 + 4g + i for the i-th word of the runs.
+      // Virtual k pairs t / t + 4 of the first MMA are real pairs 0 / 1 of that
+      // packed row, of the second MMA pairs 2 / 3, so the B fragment of lane
+      // (g, t) is the staged activation row g, values 8 (step + t) .. + 7.
+      const int g = lane >> 2, t = lane & 3;
+      constexpr uint32_t kC0 = XBF16 ? 0x43084308u : 0x64086408u;  // 136 (bf16) / 1032 (fp16)
+      constexpr uint32_t kC1 = XBF16 ? 0x43084308u : 0x64806480u;  // 136 (bf16) / 1152 (fp16)
+      float tot[2][4][4], c[2][4][4], cv[4];
 #pragma unroll
-        for (int u = 0; u < kRowsPerWarp; ++u)
-          q[u] = *reinterpret_cast<const uint4*>(src + (rr0 + u) * (kRCols * 4) + lane * 16);
-        const int lrow = s * Cfg::kStageRows + rr0;  // slice-local packed row
-        const int grp = ((kr0 + lrow) * 8) / G - g0;
-        const uint2 sv = *reinterpret_cast<const uint2*>(ssm + grp * kRCols + lane * 4);
-        float sc[4];
-        sc[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFF)));
-        sc[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
-        sc[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFF)));
-        sc[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
-        const XS* xc = xs + lrow * 8;
-        if constexpr (PATH == kRHalf2) {
-          __half2 h[4][MT];
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int m = 0; m < MT; ++m) h[c][m] = __float2half2_rn(0.f);
+          for (int r = 0; r < 4; ++r) tot[h][i][r] = c[h][i][r] = 0.f;
 #pragma unroll
-          for (int u = 0; u < kRowsPerWarp; ++u) {
-            const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-            __half2 wv[4][4];
+      for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+      for (int s = 0; s < nst; ++s) {
+        const int slot = s % stages;
+        if (!mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) break;
+        const int rows_here = min(Cfg::kStageRows, nrows - s * Cfg::kStageRows);
+        const int rr0 = warp * kRowsPerWarp;
+        const int rend = min(rr0 + kRowsPerWarp, rows_here);
+        const unsigned char* stage_base = ring + static_cast<size_t>(slot) * Cfg::kStageBytes;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) decode8_f16(words[c], wv[c]);
+        for (int step = 0; step < kRowsPerWarp / 4; ++step) {
+          const int row = rr0 + 4 * step;
+          if (row >= rend) break;
+          const unsigned char* src = stage_base + (row + t) * (kRCols * 4);
+          uint4 w[4];
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              const uint4 xv = *reinterpret_cast<const uint4*>(xc + m * xstride + u * 8);
-              const __half2 xh[4] = {h2_from_bits(xv.x), h2_from_bits(xv.y), h2_from_bits(xv.z),
-                                     h2_from_bits(xv.w)};
+          for (int h = 0; h < 2; ++h) {
+            w[2 * h] = *reinterpret_cast<const uint4*>(src + (64 * h + 4 * g) * 4);
+            w[2 * h + 1] = *reinterpret_cast<const uint4*>(src + (64 * h + 32 + 4 * g) * 4);
+          }
+          const int lrow = s * Cfg::kStageRows + row;  // slice-local packed row of the step
+          uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+          if (g < MT) xv = *reinterpret_cast<const uint4*>(xs + g * xstride + (lrow + t) * 8);
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t wa[4] = {w[2 * h].x, w[2 * h].y, w[2 * h].z, w[2 * h].w};
+            const uint32_t wb[4] = {w[2 * h + 1].x, w[2 * h + 1].y, w[2 * h + 1].z, w[2 * h + 1].w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) h[c][m] = __hfma2(wv[c][i], xh[i], h[c][m]);
+            for (int i = 0; i < 4; ++i) {
+              uint32_t ha[4], hb[4];
+              decode_mma_operands<XBF16>(wa[i], ha);
+              decode_mma_operands<XBF16>(wb[i], hb);
+              ring_mma<XBF16>(c[h][i], ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
+              ring_mma<XBF16>(c[h][i], ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
             }
           }
+          ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.x, xv.y);
+          ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.z, xv.w);
+          // flush at the end of a quantisation group or of this warp's rows
+          const int gnext = kr0 + lrow + 4;
+          if ((gnext * 8) % G == 0 || row + 4 >= rend) {
+            const int grp = ((kr0 + lrow) * 8) / G - g0;
+            const __half* sg = ssm + grp * kRCols;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+            for (int h = 0; h < 2; ++h) {
+              const uint2 sa = *reinterpret_cast<const uint2*>(sg + 64 * h + 4 * g);
+              const uint2 sb = *reinterpret_cast<const uint2*>(sg + 64 * h + 32 + 4 * g);
+              const float2 a01 = __half22float2(h2_from_bits(sa.x)), a23 = __half22float2(h2_from_bits(sa.y));
+              const float2 b01 = __half22float2(h2_from_bits(sb.x)), b23 = __half22float2(h2_from_bits(sb.y));
+              const float fa[4] = {a01.x, a01.y, a23.x, a23.y};
+              const float fb[4] = {b01.x, b01.y, b23.x, b23.y};
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              const float2 f = __half22float2(h[c][m]);
-              acc[c][m] = fmaf(f.x + f.y, sc[c], acc[c][m]);
+              for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                  if (MT == 1 && (r & 1)) continue;  // token 2t + 1 >= 1: nothing to keep
+                  tot[h][i][r] = fmaf(r < 2 ? fa[i] : fb[i], c[h][i][r] - cv[r & 1], tot[h][i][r]);
+                  c[h][i][r] = 0.f;
+                }
             }
-        } else {
-          f2 a2[4][MT];
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) a2[c][m] = f2_make(0.f, 0.f);
-#pragma unroll
-          for (int u = 0; u < kRowsPerWarp; ++u) {
-            const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-            f2 wv[4][4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const uint32_t w16 = words[c] >> 16;
-              wv[c][0] = decode_pair_f32<0>(words[c], w16);
-              wv[c][1] = decode_pair_f32<1>(words[c], w16);
-              wv[c][2] = decode_pair_f32<2>(words[c], w16);
-              wv[c][3] = decode_pair_f32<3>(words[c], w16);
-            }
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              const float4 xa = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8);
-              const float4 xb = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8 + 4);
-              const f2 xp[4] = {f2_make(xa.x, xa.y), f2_make(xa.z, xa.w), f2_make(xb.x, xb.y),
-                                f2_make(xb.z, xb.w)};
-#pragma unroll
-              for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) a2[c][m] = f2_fma(wv[c][j], xp[j], a2[c][m]);
-            }
+            for (int r = 0; r < 4; ++r) cv[r] = 0.f;
           }
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              float lo, hi;
-              f2_split(a2[c][m], lo, hi);
-              acc[c][m] = fmaf(lo + hi, sc[c], acc[c][m]);
-            }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-    }
+      // warp partials: lane (g, t) holds tokens 2t, 2t + 1 of 16 columns
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-      *reinterpret_cast<float4*>(red + (warp * MT + m) * kRCols + lane * 4) =
-          make_float4(acc[0][m], acc[1][m], acc[2][m], acc[3][m]);
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int m = 2 * t + (r & 1);
+            const int col = 64 * h + (r < 2 ? 0 : 32) + 4 * g + i;
+            if (m < MT) red[(warp * MT + m) * kRCols + col] = tot[h][i][r];
+          }
+    } else {
+      for (int s = 0; s < nst; ++s) {
+        const int slot = s % stages;
+        if (!mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) break;
+        const int rows_here = min(Cfg::kStageRows, nrows - s * Cfg::kStageRows);
+        const int rr0 = warp * kRowsPerWarp;
+        if (rr0 < rows_here) {
+          const unsigned char* src = ring + static_cast<size_t>(slot) * Cfg::kStageBytes;
+          uint4 q[kRowsPerWarp];
+  #pragma unroll
+          for (int u = 0; u < kRowsPerWarp; ++u)
+            q[u] = *reinterpret_cast<const uint4*>(src + (rr0 + u) * (kRCols * 4) + lane * 16);
+          const int lrow = s * Cfg::kStageRows + rr0;  // slice-local packed row
+          const int grp = ((kr0 + lrow) * 8) / G - g0;
+          const uint2 sv = *reinterpret_cast<const uint2*>(ssm + grp * kRCols + lane * 4);
+          float sc[4];
+          sc[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x & 0xFFFF)));
+          sc[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.x >> 16)));
+          sc[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y & 0xFFFF)));
+          sc[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(sv.y >> 16)));
+          const XS* xc = xs + lrow * 8;
+          if constexpr (PATH == kRHalf2) {
+            __half2 h[4][MT];
+  #pragma unroll
+            for (int c = 0; c < 4; ++c)
+  #pragma unroll
+              for (int m = 0; m < MT; ++m) h[c][m] = __float2half2_rn(0.f);
+  #pragma unroll
+            for (int u = 0; u < kRowsPerWarp; ++u) {
+              const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+              __half2 wv[4][4];
+  #pragma unroll
+              for (int c = 0; c < 4; ++c) decode8_f16(words[c], wv[c]);
+  #pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                const uint4 xv = *reinterpret_cast<const uint4*>(xc + m * xstride + u * 8);
+                const __half2 xh[4] = {h2_from_bits(xv.x), h2_from_bits(xv.y), h2_from_bits(xv.z),
+                                       h2_from_bits(xv.w)};
+  #pragma unroll
+                for (int c = 0; c < 4; ++c)
+  #pragma unroll
+                  for (int i = 0; i < 4; ++i) h[c][m] = __hfma2(wv[c][i], xh[i], h[c][m]);
+              }
+            }
+  #pragma unroll
+            for (int c = 0; c < 4; ++c)
+  #pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                const float2 f = __half22float2(h[c][m]);
+                acc[c][m] = fmaf(f.x + f.y, sc[c], acc[c][m]);
+              }
+          } else {
+            f2 a2[4][MT];
+  #pragma unroll
+            for (int c = 0; c < 4; ++c)
+  #pragma unroll
+              for (int m = 0; m < MT; ++m) a2[c][m] = f2_make(0.f, 0.f);
+  #pragma unroll
+            for (int u = 0; u < kRowsPerWarp; ++u) {
+              const uint32_t words[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+              f2 wv[4][4];
+  #pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const uint32_t w16 = words[c] >> 16;
+                wv[c][0] = decode_pair_f32<0>(words[c], w16);
+                wv[c][1] = decode_pair_f32<1>(words[c], w16);
+                wv[c][2] = decode_pair_f32<2>(words[c], w16);
+                wv[c][3] = decode_pair_f32<3>(words[c], w16);
+              }
+  #pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                const float4 xa = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8);
+                const float4 xb = *reinterpret_cast<const float4*>(xc + m * xstride + u * 8 + 4);
+                const f2 xp[4] = {f2_make(xa.x, xa.y), f2_make(xa.z, xa.w), f2_make(xb.x, xb.y),
+                                  f2_make(xb.z, xb.w)};
+  #pragma unroll
+                for (int c = 0; c < 4; ++c)
+  #pragma unroll
+                  for (int j = 0; j < 4; ++j) a2[c][m] = f2_fma(wv[c][j], xp[j], a2[c][m]);
+              }
+            }
+  #pragma unroll
+            for (int c = 0; c < 4; ++c)
+  #pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                float lo, hi;
+                f2_split(a2[c][m], lo, hi);
+                acc[c][m] = fmaf(lo + hi, sc[c], acc[c][m]);
+              }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+  #pragma unroll
+      for (int m = 0; m < MT; ++m)
+        *reinterpret_cast<float4*>(red + (warp * MT + m) * kRCols + lane * 4) =
+            make_float4(acc[0][m], acc[1][m], acc[2][m], acc[3][m]);
+    }
   }
   __syncthreads();
 
@@ -363,11 +519,11 @@ __global__ void __launch_bounds__(RingCfg<CW>::kThreads, 1)
 // ---------------------------------------------------------------------------
 constexpr int kCW = 8;
 
-template <int MT, bool XBF16, int PATH>
+template <int MT, bool XBF16, int PATH, int RW>
 int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N, int G,
              int splits, const DeviceInfo& dev, cudaStream_t stream) {
-  using Cfg = RingCfg<kCW>;
-  auto kern = gemv_ring_kernel<MT, XBF16, PATH, kCW>;
+  using Cfg = RingCfg<kCW, PATH, RW>;
+  auto kern = gemv_ring_kernel<MT, XBF16, PATH, kCW, RW>;
   constexpr int esz = PATH == kRFloat2 ? 4 : 2;
   const int krows = K / 8;
   const int tiles = (N + kRCols - 1) / kRCols;
@@ -383,38 +539,44 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   auto layout = [&](int stages, int rows) {
     return RingLayout(stages, Cfg::kStageBytes, MT, rows, esz, rows * 8 / G + 2, kCW);
   };
-  // Choose the K split C (cluster size): minimise the rows the busiest SM
-  // streams, assuming CTAs spread evenly over the SMs, plus a small charge per
-  // cluster rank for the DSMEM reduction.
+  // K split C (= cluster size): the largest of 1, 2, 4 that keeps the grid
+  // within one CTA per SM and at least 128 packed rows per CTA (measured on
+  // B200: a second CTA per SM, or clusters of 3, 6 or 8, cost more than they
+  // hide; thinner slices pay the fixed per-CTA cost).  Huge N: C = 1.
   int C = 1;
   if (splits > 0) {
     C = splits;
   } else {
-    long best = -1;
-    for (int c = 1; c <= kMaxRingCluster; ++c) {
-      const int rows = (((krows + c - 1) / c) + 7) / 8 * 8;
-      if (rows < 8) break;
-      const int ceff = (krows + rows - 1) / rows;
-      if (ceff != c) continue;
-      const long per_sm = static_cast<long>((tiles * c + sms - 1) / sms) * rows;
-      const long cost = per_sm + 8L * c;
-      if (best < 0 || cost < best) {
-        best = cost;
-        C = c;
-      }
-    }
+    for (int c : {2, 4})
+      if (tiles * c <= sms && krows / c >= 128) C = c;
   }
   C = std::max(1, std::min(C, std::min(kMaxRingCluster, krows / 8)));
   int rows_per_cta = (((krows + C - 1) / C) + 7) / 8 * 8;
   C = (krows + rows_per_cta - 1) / rows_per_cta;
   const int nst = (rows_per_cta + Cfg::kStageRows - 1) / Cfg::kStageRows;
+  // Shared memory: as deep a ring as fits (measured: a ring under half the SM,
+  // which would let the next kernel's CTA become resident early, is slower).
   const int ctas_per_sm = std::max(1, std::min(2, (tiles * C + sms - 1) / sms));
-  const size_t budget = smem_cap / ctas_per_sm - (ctas_per_sm > 1 ? 1024 : 0);
+  size_t budget = ctas_per_sm == 1 ? smem_cap : smem_cap / 2 - 1024;
+  if (const char* e = getenv("NG_GEMV_RING_SMEM_KB")) budget = static_cast<size_t>(atoi(e)) * 1024;
   int stages = std::min(nst, 12);
-  while (stages > 2 && layout(stages, rows_per_cta).total > budget) --stages;
+  while (stages > 1 && layout(stages, rows_per_cta).total > budget) --stages;
   if (stages < 1) stages = 1;
   if (layout(stages, rows_per_cta).total > smem_cap) return NG_ERR_BAD_SHAPE;
 
+  CUtensorMap tmap;
+  {
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encode_fn());
+    if (!enc) return NG_ERR_CUDA;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(krows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRCols), static_cast<cuuint32_t>(kBoxRows)};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(qw), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return NG_ERR_CUDA;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, C, 1);
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
@@ -429,29 +591,45 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return launch_status(cudaLaunchKernelEx(&cfg, kern, x, qw, s, y, M, K, N, G, rows_per_cta, C,
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, tmap, x, s, y, M, K, N, G, rows_per_cta, C,
                                           stages, dev.err));
 }
 
-template <bool XBF16, int PATH>
+template <bool XBF16, int PATH, int RW>
 int ring_dispatch_m(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N,
                     int G, int splits, const DeviceInfo& dev, cudaStream_t st) {
-  if (M <= 1) return run_ring<1, XBF16, PATH>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  if (M <= 2) return run_ring<2, XBF16, PATH>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  if (M <= 4) return run_ring<4, XBF16, PATH>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  return run_ring<8, XBF16, PATH>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 1) return run_ring<1, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 2) return run_ring<2, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 4) return run_ring<4, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  return run_ring<8, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
+}
+
+// Tensor-pipe consumer: packed rows per warp per stage (16 = fewest flushes,
+// 4 / 8 = smaller stages, more of them in the ring).
+template <bool XBF16>
+int ring_mma_dispatch(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K,
+                      int N, int G, int splits, const DeviceInfo& dev, cudaStream_t st) {
+  // 16 rows per warp (fewest flushes) unless the staged activations of 8
+  // rows of X leave room for only ~2 of those 64 KB stages.
+  int rw = M > 4 ? 8 : 16;
+  if (const char* e = getenv("NG_GEMV_RING_RW")) rw = atoi(e);
+  if (rw == 4) return ring_dispatch_m<XBF16, kRMma, 4>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (rw == 8) return ring_dispatch_m<XBF16, kRMma, 8>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  return ring_dispatch_m<XBF16, kRMma, 16>(x, qw, s, y, M, K, N, G, splits, dev, st);
 }
 
 }  // namespace
 
-int gemv_ring(const void* x, int x_dtype, bool float_path, const uint32_t* q, const __half* s,
+int gemv_ring(const void* x, int x_dtype, bool tensor_pipe, const uint32_t* q, const __half* s,
               void* y, int M, int K, int N, int G, int splits, const DeviceInfo& dev,
               cudaStream_t strm) {
   if (M > 8 || splits > kMaxRingCluster) return NG_ERR_BAD_ARGUMENT;
-  if (x_dtype == NG_DTYPE_BF16)
-    return ring_dispatch_m<true, kRFloat2>(x, q, s, y, M, K, N, G, splits, dev, strm);
-  if (float_path) return ring_dispatch_m<false, kRFloat2>(x, q, s, y, M, K, N, G, splits, dev, strm);
-  return ring_dispatch_m<false, kRHalf2>(x, q, s, y, M, K, N, G, splits, dev, strm);
+  if (x_dtype == NG_DTYPE_BF16) {
+    if (tensor_pipe) return ring_mma_dispatch<true>(x, q, s, y, M, K, N, G, splits, dev, strm);
+    return ring_dispatch_m<true, kRFloat2, 4>(x, q, s, y, M, K, N, G, splits, dev, strm);
+  }
+  if (tensor_pipe) return ring_mma_dispatch<false>(x, q, s, y, M, K, N, G, splits, dev, strm);
+  return ring_dispatch_m<false, kRHalf2, 4>(x, q, s, y, M, K, N, G, splits, dev, strm);
 }
 
 }  // namespace ngb

@@ -134,7 +134,7 @@ int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void
 
 
 // Bulk-copy ring GEMV (gemv_ring.cu), M <= 8; arguments already validated.
-int gemv_ring(const void* x, int x_dtype, bool float_path, const uint32_t* q, const __half* s,
+int gemv_ring(const void* x, int x_dtype, bool tensor_pipe, const uint32_t* q, const __half* s,
               void* y, int M, int K, int N, int G, int splits, const DeviceInfo& dev,
               cudaStream_t strm);
 

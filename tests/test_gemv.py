@@ -181,43 +181,49 @@ RING_CASES = [(1, 512, 256), (2, 256, 132), (3, 1024, 260), (4, 512, 512), (5, 2
 @pytest.mark.parametrize("M,K,N", RING_CASES)
 @pytest.mark.parametrize("G", [64, 128, 256])
 @pytest.mark.parametrize("act", ["f16", "bf16"])
-def test_ring_matches_oracle(M, K, N, G, act):
+@pytest.mark.parametrize("algo", [4, 5])
+def test_ring_matches_oracle(M, K, N, G, act, algo):
     if K % G:
         pytest.skip("K not a multiple of G")
     X, qw, ref = make_case(M, K, N, G, seed=M * 5 + N + G, act=act)
-    check(ng.gemv(X, qw, algo=4), ref, X.dtype)
+    check(ng.gemv(X, qw, algo=algo), ref, X.dtype)
     assert ng.extension().device_status() == 0
 
 
 @pytest.mark.parametrize("K,N", FULL + [(2048, 4096), (4096, 3072), (4096, 7168), (7168, 4096)])
 @pytest.mark.parametrize("M", [1, 8])
-def test_ring_full_size_shapes(K, N, M):
+@pytest.mark.parametrize("algo", [4, 5])
+def test_ring_full_size_shapes(K, N, M, algo):
     """BASELINE config 1 / config 2 shapes and the tensor-parallel Llama-3-8B
     shards (o / qkv / gate-up / down at TP=2), including multi-wave stage reuse."""
     X, qw, ref = make_case(M, K, N, 128, seed=K + N + M)
-    check(ng.gemv(X, qw, algo=4), ref, torch.float16)
+    check(ng.gemv(X, qw, algo=algo), ref, torch.float16)
     assert ng.extension().device_status() == 0
 
 
 @pytest.mark.parametrize("splits", [1, 2, 3, 5, 8])
-def test_ring_split_invariance(splits):
+@pytest.mark.parametrize("algo", [4, 5])
+def test_ring_split_invariance(splits, algo):
     X, qw, ref = make_case(2, 4096, 1028, 128, seed=splits)
-    y = ng.gemv(X, qw, splits=splits, algo=4)
+    y = ng.gemv(X, qw, splits=splits, algo=algo)
     check(y, ref, torch.float16)
-    assert torch.equal(y, ng.gemv(X, qw, splits=splits, algo=4))
+    assert torch.equal(y, ng.gemv(X, qw, splits=splits, algo=algo))
 
 
 def test_ring_output_fully_written_and_rejects_m_above_8():
     X, qw, ref = make_case(3, 1024, 1028, 128, seed=8)
     out = torch.full((3, 1028), float("nan"), dtype=torch.float16, device="cuda")
-    ng.extension().gemv_w4a16(X, qw.qweight, qw.scales, 128, algo=4, out=out)
-    check(out, ref, torch.float16)
+    for algo in (4, 5):
+        out.fill_(float("nan"))
+        ng.extension().gemv_w4a16(X, qw.qweight, qw.scales, 128, algo=algo, out=out)
+        check(out, ref, torch.float16)
     X9, qw9, _ = make_case(9, 256, 128, 128)
     with pytest.raises(Exception):
         ng.gemv(X9, qw9, algo=4)
 
 
-def test_ring_back_to_back_in_graph():
+@pytest.mark.parametrize("algo", [4, 5])
+def test_ring_back_to_back_in_graph(algo):
     """A chain of ring GEMVs captured in one CUDA graph (programmatic dependent
     launch between them): each output still matches its own oracle."""
     cases = [make_case(1, K, N, 128, seed=K + N) for K, N in [(4096, 14336), (14336, 4096), (4096, 4096)]]
@@ -229,7 +235,7 @@ def test_ring_back_to_back_in_graph():
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for (X, qw, _), o in zip(cases, outs):
-                ext.gemv_w4a16(X, qw.qweight, qw.scales, 128, algo=4, out=o)
+                ext.gemv_w4a16(X, qw.qweight, qw.scales, 128, algo=algo, out=o)
     torch.cuda.current_stream().wait_stream(s)
     for _ in range(3):
         g.replay()
