@@ -98,7 +98,8 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
  *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x).
  *   - algo 0 (default): algo 5 below when M <= 8, block_threads == 0,
- *     splits <= 8 and either the packed weight is >= 12 MiB or M > 4;
+ *     splits <= 8 and either M > 4 or the packed weight is >= 12 MiB (at
+ *     M = 1 also K <= 4096);
  *     otherwise algo 1 (fp16 x) / algo 2 (bf16 x).
  *   - bulk-copy ring (algo 4 / 5; M <= 8; the workspace is not used): one
  *     producer warp per CTA streams the CTA's (128-column, K-slice) weight

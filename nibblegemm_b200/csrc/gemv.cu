@@ -419,13 +419,14 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
       return gemv_tc(x, x_dtype, q, s, y, M, K, N, group_size, workspace, dev, strm);
     }
   }
-  // Default schedule: the tensor-pipe ring for large weights (>= 12 MB) or
-  // M > 4, the cluster kernel otherwise (measured crossover on B200).  A
+  // Default schedule: the tensor-pipe ring for large weights (>= 12 MB; at
+  // M = 1 only for K <= 4096, where its one-slice-per-tile grid is shallow)
+  // or M > 4, the cluster kernel otherwise (measured crossover on B200).  A
   // block width, or a split count above the ring's cluster limit, selects the
   // cluster kernel (those options are its own).
   const double wbytes = static_cast<double>(K) * N / 2.0;
   if (algo == 0 && M <= 8 && block_threads == 0 && splits <= 8 &&
-      (wbytes >= 12.0 * (1 << 20) || M > 4))
+      ((wbytes >= 12.0 * (1 << 20) && (M > 1 || K <= 4096)) || M > 4))
     algo = 5;
   if (algo >= 4)
     return gemv_ring(x, x_dtype, algo == 5, q, s, y, M, K, N, group_size, splits, dev, strm);

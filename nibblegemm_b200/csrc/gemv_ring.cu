@@ -116,13 +116,13 @@ template <bool BF16>
 __device__ __forceinline__ void ring_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
   if constexpr (BF16) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -558,7 +558,6 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   // which would let the next kernel's CTA become resident early, is slower).
   const int ctas_per_sm = std::max(1, std::min(2, (tiles * C + sms - 1) / sms));
   size_t budget = ctas_per_sm == 1 ? smem_cap : smem_cap / 2 - 1024;
-  if (const char* e = getenv("NG_GEMV_RING_SMEM_KB")) budget = static_cast<size_t>(atoi(e)) * 1024;
   int stages = std::min(nst, 12);
   while (stages > 1 && layout(stages, rows_per_cta).total > budget) --stages;
   if (stages < 1) stages = 1;
@@ -612,7 +611,6 @@ int ring_mma_dispatch(const void* x, const uint32_t* qw, const __half* s, void* 
   // 16 rows per warp (fewest flushes) unless the staged activations of 8
   // rows of X leave room for only ~2 of those 64 KB stages.
   int rw = M > 4 ? 8 : 16;
-  if (const char* e = getenv("NG_GEMV_RING_RW")) rw = atoi(e);
   if (rw == 4) return ring_dispatch_m<XBF16, kRMma, 4>(x, qw, s, y, M, K, N, G, splits, dev, st);
   if (rw == 8) return ring_dispatch_m<XBF16, kRMma, 8>(x, qw, s, y, M, K, N, G, splits, dev, st);
   return ring_dispatch_m<XBF16, kRMma, 16>(x, qw, s, y, M, K, N, G, splits, dev, st);
