@@ -97,17 +97,20 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     order; block_threads 0 (256), 128 or 256;  algo 1 = fp16 decode with
  *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
  *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x).
- *   - algo 0 (default): algo 5 below when M <= 8, block_threads == 0,
- *     splits <= 8 and either M > 4 or the packed weight is >= 12 MiB (at
- *     M = 1 also K <= 4096);
- *     otherwise algo 1 (fp16 x) / algo 2 (bf16 x).
- *   - bulk-copy ring (algo 4 / 5; M <= 8; the workspace is not used): one
- *     producer warp per CTA streams the CTA's (128-column, K-slice) weight
- *     block into a shared-memory ring with cp.async.bulk, consumer warps
+ *   - algo 0 (default), with block_threads == 0 and splits <= 8, M <= 8:
+ *     algo 5 with one K slice per column tile when N >= 12288 and (M >= 2 or
+ *     K <= 4096); algo 5 (stream-K) when M is 3..4 and the packed weight is
+ *     >= 12 MiB; algo 5 when M > 4; otherwise algo 1 (fp16 x) / 2 (bf16 x).
+ *   - bulk-copy ring (algo 4 / 5; M <= 8; the workspace only for stream-K):
+ *     one producer warp per CTA streams the CTA's (128-column, K-slice) weight
+ *     block into a shared-memory ring with 2-D TMA loads, consumer warps
  *     decode from shared memory -- algo 4 with the algo 1 (fp16 x) / algo 2
  *     (bf16 x) arithmetic, algo 5 on the tensor pipe (magic-number operands to
  *     mma.sync, fp32 accumulation, offsets removed by a correction MMA);
- *     `splits` 1..8 or 0 = heuristic, K slices reduced in a cluster as above.
+ *     `splits` 1..8 = K slices reduced in a cluster as above; 0 = algo 5 on
+ *     M <= 4 with K % 128 == 0 and a workspace: stream-K (one CTA per SM,
+ *     equal shares of 16-row blocks, split tiles finished through the
+ *     workspace in CTA order); otherwise a heuristic K split.
  *   All are launched with programmatic stream serialisation: they start
  *   streaming their read-only weights while the previous kernel on the stream
  *   finishes, and read x / write y / touch the workspace only after it has.
@@ -118,8 +121,8 @@ int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint
                   int algo, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Workspace bytes the tensor-pipe GEMV needs for an N-column weight on the
- * current device (0 if M or N is out of range).  No counterpart in the
+ * Workspace bytes ng_gemv_w4a16 needs for an N-column weight on the current
+ * device, every schedule included (0 if M or N is out of range).  No counterpart in the
  * reference, which allocates its workspace inside each call.
  */
 size_t ng_gemv_workspace_bytes(int M, int N);

@@ -419,17 +419,25 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
       return gemv_tc(x, x_dtype, q, s, y, M, K, N, group_size, workspace, dev, strm);
     }
   }
-  // Default schedule: the tensor-pipe ring for large weights (>= 12 MB; at
-  // M = 1 only for K <= 4096, where its one-slice-per-tile grid is shallow)
-  // or M > 4, the cluster kernel otherwise (measured crossover on B200).  A
-  // block width, or a split count above the ring's cluster limit, selects the
-  // cluster kernel (those options are its own).
-  const double wbytes = static_cast<double>(K) * N / 2.0;
-  if (algo == 0 && M <= 8 && block_threads == 0 && splits <= 8 &&
-      ((wbytes >= 12.0 * (1 << 20) && (M > 1 || K <= 4096)) || M > 4))
-    algo = 5;
+  // Default schedule (measured on B200, M <= 8, no cluster-kernel options):
+  //   * >= 96 column tiles (N >= 12288) and M >= 2 or K <= 4096: the ring with
+  //     one CTA per tile (its CTAs sweep the rows in lockstep);
+  //   * M = 3..4 and a packed weight >= 12 MiB: the stream-K ring (all SMs);
+  //   * M > 4: the ring with its own K split;
+  //   * otherwise the cluster kernel.
+  if (algo == 0 && M <= 8 && block_threads == 0 && splits <= 8) {
+    const int tiles = (N + 127) / 128;
+    const double wbytes = static_cast<double>(K) * N / 2.0;
+    if (tiles >= 96 && (M > 1 || K <= 4096)) {
+      algo = 5;
+      if (splits == 0) splits = 1;
+    } else if (M > 4 || (M >= 3 && wbytes >= 12.0 * (1 << 20))) {
+      algo = 5;
+    }
+  }
   if (algo >= 4)
-    return gemv_ring(x, x_dtype, algo == 5, q, s, y, M, K, N, group_size, splits, dev, strm);
+    return gemv_ring(x, x_dtype, algo == 5, q, s, y, M, K, N, group_size, splits, workspace,
+                     workspace_bytes, dev, strm);
   const int threads = block_threads ? block_threads : 256;
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_w<true, kFloat2>(threads, x, q, s, y, M, K, N, group_size, splits, dev, strm);
@@ -441,5 +449,5 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
 extern "C" size_t ng_gemv_workspace_bytes(int M, int N) {
   ngb::DeviceInfo dev;
   if (M < 1 || M > 16 || N <= 0 || ngb::current_device_info(&dev) != NG_OK) return 0;
-  return ngb::gemv_tc_workspace_bytes(N, dev);
+  return ngb::gemv_ring_workspace_bytes(N, dev);
 }

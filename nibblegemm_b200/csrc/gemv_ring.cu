@@ -514,6 +514,319 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
   cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
+
+// ---------------------------------------------------------------------------
+// Stream-K ring (tensor-pipe consumer; M <= 4; X fits on chip; workspace).
+//
+// The grid above gives each 128-column tile the same K split, so a shape with
+// T tiles keeps only T x C of the 148 SMs busy (config 1: 112).  Here the
+// work is the list of 16-row blocks in tile-major order, split into equal
+// contiguous ranges over one persistent CTA per SM.  Each stage holds up to 8
+// consecutive blocks of one tile (consumer warp w takes block w, exactly the
+// per-warp arithmetic of the ring above).  When a CTA's range leaves a tile it
+// reduces its warps' partials for that tile (a "segment"):
+//   * a segment covering the whole tile is written to Y directly;
+//   * a segment that starts inside the tile (only a CTA's first segment can)
+//     is published to the workspace: partial sums, then a flag (release);
+//   * a segment that starts at the tile's first row but stops short is
+//     finished by this CTA: it waits (bounded) for the flags of the later
+//     CTAs holding the rest of the tile, adds their partials in CTA order
+//     (deterministic), writes Y and clears the flags.
+// A CTA reaches the tile it finishes at the end of its range, while the later
+// CTAs publish theirs at the start of their ranges, so the wait is short and
+// never circular.  The grid is at most one CTA per SM, so all CTAs become
+// resident once the previous kernel drains.
+// Measured trade-off: CTAs here stream different rows at the same time,
+// which costs DRAM locality against the clustered grid (whose CTAs sweep the
+// matrix rows in lockstep); it wins where the clustered grid would leave most
+// SMs idle (few column tiles, long K) at M = 3..4.
+// ---------------------------------------------------------------------------
+constexpr int kSkRB = 16;                          // packed rows per block
+constexpr int kSkCW = 8;                           // consumer warps
+constexpr int kSkStageRows = kSkCW * kSkRB;        // 128
+constexpr int kSkStageBytes = kSkStageRows * kRCols * 4;
+constexpr int kSkThreads = (kSkCW + 1) * 32;
+constexpr int kSkMaxM = 4;
+
+struct SkPart {  // U blocks over P CTAs: the first r get q + 1, the rest q
+  int q, r;
+  __host__ __device__ int start(int b) const { return b * q + (b < r ? b : r); }
+  __host__ __device__ int owner(int u) const {
+    const int big = r * (q + 1);
+    return u < big ? u / (q + 1) : r + (u - big) / q;
+  }
+};
+
+struct SkLayout {
+  size_t ring, xs, sc, red, fin, total;
+  __host__ __device__ SkLayout(int stages, int MT, int K, int groups) {
+    size_t off = 1024;
+    ring = off;
+    off += static_cast<size_t>(stages) * kSkStageBytes;
+    xs = off;
+    off += (static_cast<size_t>(MT) * K * 2 + 15) / 16 * 16;
+    sc = off;
+    off += static_cast<size_t>(groups) * kRCols * 2;
+    red = off;
+    off += static_cast<size_t>(kSkCW) * MT * kRCols * 4;
+    fin = off;
+    off += static_cast<size_t>(MT) * kRCols * 4;
+    total = off;
+  }
+};
+
+__device__ __forceinline__ unsigned int sk_ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void sk_st_release(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int MT, bool XBF16>
+__global__ void __launch_bounds__(kSkThreads, 1)
+    gemv_ring_sk_kernel(const __grid_constant__ CUtensorMap tmap_q, const void* __restrict__ x,
+                        const __half* __restrict__ scales, void* __restrict__ y, int M, int K,
+                        int N, int G, SkPart part, int stages, int sc_groups,
+                        float* __restrict__ ws_part, unsigned int* __restrict__ ws_flag,
+                        unsigned int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + stages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + stages);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int krows = K >> 3;
+  const int RT = krows / kSkRB;  // blocks per tile
+  const int b = blockIdx.x;
+  const int u0 = part.start(b), u1 = part.start(b + 1);
+  const int GR = G / 8;  // packed rows per quantisation group
+  const int lg0 = (u0 * kSkRB) / GR;  // first linear (tile-major) group of the range
+  const int nlg = u1 > u0 ? (u1 * kSkRB - 1) / GR - lg0 + 1 : 0;
+  const SkLayout L(stages, MT, K, sc_groups);
+  unsigned char* ring = smem + L.ring;
+  __half* xs = reinterpret_cast<__half*>(smem + L.xs);
+  __half* ssm = reinterpret_cast<__half*>(smem + L.sc);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* fin = reinterpret_cast<float*>(smem + L.fin);
+
+  if (tid == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kSkCW);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == kSkCW) {
+    // ---------------- producer ----------------
+    const uint64_t pol = make_evict_first_policy();
+    int s = 0, issued = 0;
+    for (int u = u0; u < u1; ++s) {
+      const int tile = u / RT, rb = u - tile * RT;
+      const int n = min(kSkCW, min(RT - rb, u1 - u));
+      const int slot = s % stages;
+      if (s >= stages) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((s / stages) - 1) & 1, err, abort_flag);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      }
+      const int boxes = n * (kSkRB / kBoxRows);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], boxes * (kBoxRows * kRCols * 4));
+      __syncwarp();
+      unsigned char* dst = ring + static_cast<size_t>(slot) * kSkStageBytes;
+      if (lane < boxes)
+        tma_box_g2s(dst + lane * (kBoxRows * kRCols * 4), &tmap_q, &full[slot], tile * kRCols,
+                    rb * kSkRB + lane * kBoxRows, pol);
+      issued = s + 1;
+      u += n;
+    }
+    if (lane == 0)
+      for (int t = max(0, issued - stages); t < issued; ++t)
+        mbar_wait_drain(&full[t % stages], (t / stages) & 1, err);
+    return;  // segment barriers below are consumer-only (named barrier 1)
+  }
+
+  // ---------------- consumers ----------------
+  for (int i = tid; i < nlg * 32; i += kSkCW * 32) {
+    const int g = i >> 5, l = i & 31;
+    const int LG = lg0 + g;
+    const int tile = LG / (K / G), gi = LG - tile * (K / G);
+    const int col = tile * kRCols + l * 4;
+    if (col < N) cp_async_8(ssm + g * kRCols + l * 4, scales + static_cast<size_t>(gi) * N + col);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  {
+    const unsigned short* xin = static_cast<const unsigned short*>(x);
+    for (int i = tid; i < MT * krows; i += kSkCW * 32) {
+      const int m = i / krows, r = i - m * krows;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (m < M) v = ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(r) * 8);
+      if constexpr (!XBF16) {
+        const __half2 sixteenth = __float2half2_rn(0.0625f);
+        v.y = h2_bits(__hmul2(h2_from_bits(v.y), sixteenth));
+        v.w = h2_bits(__hmul2(h2_from_bits(v.w), sixteenth));
+      }
+      *reinterpret_cast<uint4*>(xs + static_cast<size_t>(m) * K + r * 8) = v;
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
+
+  const int g = lane >> 2, t = lane & 3;
+  constexpr uint32_t kC0 = XBF16 ? 0x43084308u : 0x64086408u;
+  constexpr uint32_t kC1 = XBF16 ? 0x43084308u : 0x64806480u;
+  float tot[2][4][4], c[2][4][4], cv[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) tot[h][i][r] = c[h][i][r] = 0.f;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+
+  constexpr int E = MT * kRCols;
+  int s = 0;
+  bool aborted = false;
+  for (int u = u0; u < u1; ++s) {
+    const int tile = u / RT, rb = u - tile * RT;
+    const int n = min(kSkCW, min(RT - rb, u1 - u));
+    const int slot = s % stages;
+    if (!aborted && !mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) aborted = true;
+    if (!aborted && warp < n) {
+      const int row0 = (rb + warp) * kSkRB;  // tile row of this warp's block
+      const unsigned char* blk = ring + static_cast<size_t>(slot) * kSkStageBytes +
+                                 warp * (kSkRB * kRCols * 4);
+#pragma unroll
+      for (int step = 0; step < kSkRB / 4; ++step) {
+        const int row = row0 + 4 * step;
+        const unsigned char* src = blk + (4 * step + t) * (kRCols * 4);
+        uint4 w[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          w[2 * h] = *reinterpret_cast<const uint4*>(src + (64 * h + 4 * g) * 4);
+          w[2 * h + 1] = *reinterpret_cast<const uint4*>(src + (64 * h + 32 + 4 * g) * 4);
+        }
+        uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+        if (g < MT) xv = *reinterpret_cast<const uint4*>(xs + static_cast<size_t>(g) * K + (row + t) * 8);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t wa[4] = {w[2 * h].x, w[2 * h].y, w[2 * h].z, w[2 * h].w};
+          const uint32_t wb[4] = {w[2 * h + 1].x, w[2 * h + 1].y, w[2 * h + 1].z, w[2 * h + 1].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t ha[4], hb[4];
+            decode_mma_operands<XBF16>(wa[i], ha);
+            decode_mma_operands<XBF16>(wb[i], hb);
+            ring_mma<XBF16>(c[h][i], ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
+            ring_mma<XBF16>(c[h][i], ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
+          }
+        }
+        ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.x, xv.y);
+        ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.z, xv.w);
+        if ((row + 4) % GR == 0 || step == kSkRB / 4 - 1) {  // group or block end
+          const int lg = ((tile * krows + row) * 8) / G - lg0;
+          const __half* sg = ssm + lg * kRCols;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint2 sa = *reinterpret_cast<const uint2*>(sg + 64 * h + 4 * g);
+            const uint2 sb = *reinterpret_cast<const uint2*>(sg + 64 * h + 32 + 4 * g);
+            const float2 a01 = __half22float2(h2_from_bits(sa.x)), a23 = __half22float2(h2_from_bits(sa.y));
+            const float2 b01 = __half22float2(h2_from_bits(sb.x)), b23 = __half22float2(h2_from_bits(sb.y));
+            const float fa[4] = {a01.x, a01.y, a23.x, a23.y};
+            const float fb[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                if (MT == 1 && (r & 1)) continue;
+                tot[h][i][r] = fmaf(r < 2 ? fa[i] : fb[i], c[h][i][r] - cv[r & 1], tot[h][i][r]);
+                c[h][i][r] = 0.f;
+              }
+          }
+#pragma unroll
+          for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+
+    if (rb + n == RT || u + n == u1) {
+      // ---- segment end: this CTA's share of `tile` is complete ----
+      const int t0 = tile * RT;
+      const bool starts_at_0 = u0 <= t0;
+      const bool whole = starts_at_0 && u1 >= t0 + RT;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int m = 2 * t + (r & 1);
+            const int col = 64 * h + (r < 2 ? 0 : 32) + 4 * g + i;
+            if (m < MT) red[(warp * MT + m) * kRCols + col] = tot[h][i][r];
+            tot[h][i][r] = 0.f;
+          }
+      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (1) warp partials visible
+      unsigned short* yo = static_cast<unsigned short*>(y);
+      auto store = [&](int e, float v) {
+        const int m = e / kRCols, cn = tile * kRCols + (e % kRCols);
+        if (m < M && cn < N)
+          yo[static_cast<size_t>(m) * N + cn] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                      : __half_as_ushort(__float2half_rn(v));
+      };
+      for (int e = tid; e < E; e += kSkCW * 32) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kSkCW; ++w) v += red[w * E + e];
+        if (whole)
+          store(e, v);
+        else if (starts_at_0)
+          fin[e] = v;
+        else
+          ws_part[static_cast<size_t>(b) * (kSkMaxM * kRCols) + e] = v;
+      }
+      if (!whole && !starts_at_0) __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (2)
+      if (!whole && !starts_at_0) {
+        if (tid == 0) sk_st_release(&ws_flag[b], 1u);
+      } else if (!whole) {
+        // finisher: the later CTAs holding the rest of the tile
+        const int last = part.owner(t0 + RT - 1);
+        if (tid == 0) {
+          for (int o = b + 1; o <= last; ++o) {
+            const uint64_t ts = global_timer_ns();
+            while (sk_ld_acquire(&ws_flag[o]) == 0u) {
+              if (global_timer_ns() - ts > 1000000000ull) {
+                atomicOr(err, kErrWaitTimeout);
+                break;
+              }
+            }
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
+        for (int e = tid; e < E; e += kSkCW * 32) {
+          float v = fin[e];
+          for (int o = b + 1; o <= last; ++o) v += __ldcg(ws_part + static_cast<size_t>(o) * (kSkMaxM * kRCols) + e);
+          store(e, v);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
+        if (tid == 0)
+          for (int o = b + 1; o <= last; ++o) ws_flag[o] = 0u;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (3) red / fin reusable
+    }
+    u += n;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -616,12 +929,101 @@ int ring_mma_dispatch(const void* x, const uint32_t* qw, const __half* s, void* 
   return ring_dispatch_m<XBF16, kRMma, 16>(x, qw, s, y, M, K, N, G, splits, dev, st);
 }
 
+
+// Workspace of the stream-K ring: partial sums then flags, after the region
+// the tensor-pipe persistent GEMV (algo 3) uses, so the two never overlap.
+size_t sk_ws_offset(int N, const DeviceInfo& dev) {
+  return (gemv_tc_workspace_bytes(N, dev) + 255) / 256 * 256;
+}
+size_t sk_ws_bytes(const DeviceInfo& dev) {
+  return static_cast<size_t>(dev.sm_count) * (kSkMaxM * kRCols * 4 + 4);
+}
+
+// Returns NG_OK, an error, or -1 when the stream-K variant does not apply.
+template <int MT, bool XBF16>
+int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N,
+                int G, void* ws, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
+  const int krows = K / 8;
+  if (krows % kSkRB != 0) return -1;
+  if (static_cast<size_t>(MT) * K * 2 > 64 * 1024) return -1;
+  const size_t off = sk_ws_offset(N, dev);
+  if (ws == nullptr || ws_bytes < off + sk_ws_bytes(dev)) return -1;
+  const int RT = krows / kSkRB;
+  const int tiles = (N + kRCols - 1) / kRCols;
+  const int U = tiles * RT;
+  const int P = std::min(dev.sm_count, U);
+  SkPart part{U / P, U % P};
+  const int sc_groups = ((part.q + 1) * kSkRB) / (G / 8) + 2;
+  const size_t smem_cap = dev.smem_optin ? dev.smem_optin : 227 * 1024;
+  const int want = (part.q + 1 + kSkCW - 1) / kSkCW + 1;  // stages a range can span
+  int stages = std::min(4, want);
+  while (stages > 1 && SkLayout(stages, MT, K, sc_groups).total > smem_cap) --stages;
+  const size_t smem = SkLayout(stages, MT, K, sc_groups).total;
+  if (smem > smem_cap) return -1;
+
+  auto kern = gemv_ring_sk_kernel<MT, XBF16>;
+  static std::once_flag once[64];
+  std::call_once(once[dev.device], [&] {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_cap));
+  });
+  CUtensorMap tmap;
+  {
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encode_fn());
+    if (!enc) return NG_ERR_CUDA;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(krows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRCols), static_cast<cuuint32_t>(kBoxRows)};
+    const cuuint32_t es[2] = {1, 1};
+    if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(qw), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return NG_ERR_CUDA;
+  }
+  float* ws_part = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + off);
+  unsigned int* ws_flag = reinterpret_cast<unsigned int*>(ws_part + static_cast<size_t>(dev.sm_count) * kSkMaxM * kRCols);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(P, 1, 1);
+  cfg.blockDim = dim3(kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  // Not a cooperative launch: the grid is at most one CTA per SM and every
+  // wait is bounded, and a cooperative launch was measured to gain nothing.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, tmap, x, s, y, M, K, N, G, part, stages,
+                                          sc_groups, ws_part, ws_flag, dev.err));
+}
+
+template <bool XBF16>
+int ring_sk_dispatch(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N,
+                     int G, void* ws, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t st) {
+  if (M <= 1) return run_ring_sk<1, XBF16>(x, qw, s, y, M, K, N, G, ws, ws_bytes, dev, st);
+  if (M <= 2) return run_ring_sk<2, XBF16>(x, qw, s, y, M, K, N, G, ws, ws_bytes, dev, st);
+  if (M <= 4) return run_ring_sk<4, XBF16>(x, qw, s, y, M, K, N, G, ws, ws_bytes, dev, st);
+  return -1;
+}
+
 }  // namespace
 
+size_t gemv_ring_workspace_bytes(int N, const DeviceInfo& dev) {
+  return sk_ws_offset(N, dev) + sk_ws_bytes(dev);
+}
+
 int gemv_ring(const void* x, int x_dtype, bool tensor_pipe, const uint32_t* q, const __half* s,
-              void* y, int M, int K, int N, int G, int splits, const DeviceInfo& dev,
-              cudaStream_t strm) {
+              void* y, int M, int K, int N, int G, int splits, void* ws, size_t ws_bytes,
+              const DeviceInfo& dev, cudaStream_t strm) {
   if (M > 8 || splits > kMaxRingCluster) return NG_ERR_BAD_ARGUMENT;
+  // Stream-K over all SMs when it applies (tensor pipe, M <= 4, X on chip, a
+  // workspace, no explicit split); the clustered K split otherwise.
+  if (tensor_pipe && splits == 0 && M <= kSkMaxM) {
+    const int st = x_dtype == NG_DTYPE_BF16
+                       ? ring_sk_dispatch<true>(x, q, s, y, M, K, N, G, ws, ws_bytes, dev, strm)
+                       : ring_sk_dispatch<false>(x, q, s, y, M, K, N, G, ws, ws_bytes, dev, strm);
+    if (st != -1) return st;
+  }
   if (x_dtype == NG_DTYPE_BF16) {
     if (tensor_pipe) return ring_mma_dispatch<true>(x, q, s, y, M, K, N, G, splits, dev, strm);
     return ring_dispatch_m<true, kRFloat2, 4>(x, q, s, y, M, K, N, G, splits, dev, strm);

@@ -135,8 +135,11 @@ int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void
 
 // Bulk-copy ring GEMV (gemv_ring.cu), M <= 8; arguments already validated.
 int gemv_ring(const void* x, int x_dtype, bool tensor_pipe, const uint32_t* q, const __half* s,
-              void* y, int M, int K, int N, int G, int splits, const DeviceInfo& dev,
-              cudaStream_t strm);
+              void* y, int M, int K, int N, int G, int splits, void* ws, size_t ws_bytes,
+              const DeviceInfo& dev, cudaStream_t strm);
+// Workspace bytes ng_gemv_w4a16 needs for every schedule (tensor-pipe
+// persistent GEMV region, then the stream-K ring's partials and flags).
+size_t gemv_ring_workspace_bytes(int N, const DeviceInfo& dev);
 
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

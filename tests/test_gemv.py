@@ -243,3 +243,23 @@ def test_ring_back_to_back_in_graph(algo):
     for (_, _, ref), o in zip(cases, outs):
         check(o, ref, torch.float16)
     assert ext.device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N,G", [(1, 4096, 14336, 128), (2, 14336, 4096, 128), (4, 4096, 4096, 64),
+                                     (1, 2048, 4100, 256), (3, 1024, 132, 128), (1, 8192, 8192, 128)])
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+def test_ring_stream_k_matches_oracle_and_leaves_flags_zero(M, K, N, G, act):
+    """The stream-K ring (algo 5, no explicit split, M <= 4): parity, run-to-run
+    determinism, and the per-CTA flags in the workspace back at zero."""
+    X, qw, ref = make_case(M, K, N, G, seed=M + K + N + G, act=act)
+    ext = ng.extension()
+    y = ext.gemv_w4a16(X, qw.qweight, qw.scales, G, algo=5)
+    check(y, ref, X.dtype)
+    for _ in range(3):
+        assert torch.equal(y, ext.gemv_w4a16(X, qw.qweight, qw.scales, G, algo=5))
+    torch.cuda.synchronize()
+    assert ext.device_status() == 0
+    ws = ext.workspace(N, X.device, torch.cuda.current_stream().cuda_stream)
+    total = ext.lib.ng_gemv_workspace_bytes(1, N)
+    sm = torch.cuda.get_device_properties(X.device).multi_processor_count
+    assert int(ws[total - 4 * sm: total].count_nonzero()) == 0
