@@ -140,7 +140,11 @@ class ProjectionStackStep:
         for layer in self.proj:
             for p in layer:
                 if p.x.size(0) <= 16:
-                    ext.gemv_w4a16(p.x, p.weight.qweight, p.weight.scales, p.weight.group_size, out=p.y)
+                    # The cluster GEMV (algo 1 fp16 / 2 bf16): measured fastest in
+                    # this mixed chain of shapes, where the ring kernels' 219 KB
+                    # CTAs keep the next projection from starting early.
+                    ext.gemv_w4a16(p.x, p.weight.qweight, p.weight.scales, p.weight.group_size,
+                                   algo=2 if p.x.dtype == torch.bfloat16 else 1, out=p.y)
                 else:
                     ext.gemm_w4a16(p.x, p.weight.qweight, p.weight.scales, p.weight.group_size, out=p.y)
                 if p.style == "row" and self.world > 1:
