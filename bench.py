@@ -49,7 +49,114 @@ WORKLOADS = {
     "gemv": dict(M=1, K=4096, N=14336, G=128, name="W4A16 decode GEMV M=1 K=4096 N=14336 g128 fp16 (BASELINE config 1)"),
     "gemm": dict(M=2048, K=4096, N=14336, G=128, name="W4A16 prefill GEMM M=2048 K=4096 N=14336 g128 fp16 (BASELINE config 3)"),
     "step8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 projection stack (224 projections), batch 1, tensor-parallel over the ranks"),
+    "sweep2": dict(M=1, K=4096, N=14336, G=128, name="BASELINE config 2: decode GEMV sweep M x (K, N), eager and graph, vs cuBLAS fp16"),
+    "sweep3": dict(M=2048, K=4096, N=14336, G=128, name="BASELINE config 3: prefill GEMM sweep M x (K, N) x {fp16, bf16}"),
 }
+
+SWEEP2_M = (1, 2, 4, 8, 16)
+SWEEP2_SHAPES = ((4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096), (8192, 8192))
+SWEEP3_M = (16, 128, 512, 2048, 8192)
+SWEEP3_SHAPES = ((4096, 14336), (14336, 4096))
+
+
+def _graph_us(fn, n, stream):
+    """Device time per call of `fn(i)`, `n` calls captured in one CUDA graph."""
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(n):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / n
+
+
+def _eager_us(fn, n):
+    """Wall-inclusive device time per call of `fn(i)` launched eagerly from Python."""
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n):
+        fn(i)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / n
+
+
+def run_sweep(args, local):
+    """BASELINE configs 2 and 3 as one JSON line per point (seeded synthetic data;
+    weights rotated over more than L2 between calls)."""
+    import nibblegemm_b200 as ng
+    from oracle import quant_oracle as qo  # seeded synthetic inputs (generator only)
+    ext = ng.extension()
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    hbm, bf16_peak, src = measured_peaks()
+    stream = torch.cuda.Stream()
+    shapes = SWEEP2_SHAPES if args.workload == "sweep2" else SWEEP3_SHAPES
+    for K, N in shapes:
+        _, q, s = qo.synthetic_case(1, K, N, group_size=128, seed=7)
+        wbytes = q.nbytes + s.nbytes
+        nrot = max(2, -(-3 * l2 // (2 * wbytes)))
+        Q = [torch.from_numpy(q).cuda() for _ in range(nrot)]
+        S = torch.from_numpy(s).cuda()
+        W16 = ext.dequant_w4(Q[0], S, 128)  # cuBLAS comparison operand (fp16 [K, N])
+        n16 = max(2, -(-3 * l2 // (2 * W16.numel() * 2)))
+        W16s = [W16] + [W16.clone() for _ in range(n16 - 1)]
+        if args.workload == "sweep2":
+            for M in SWEEP2_M:
+                X = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).half().cuda()
+                Y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+                ours = lambda i: ext.gemv_w4a16(X, Q[i % nrot], S, 128, out=Y)
+                Y16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+                cub = lambda i: torch.mm(X, W16s[i % n16], out=Y16)
+                n = 100
+                ug, ue = _graph_us(ours, n, stream), _eager_us(ours, n)
+                cg_, ce = _graph_us(cub, n, stream), _eager_us(cub, n)
+                nb = algo_bytes(M, K, N, 128)
+                b16 = K * N * 2 + M * K * 2 + M * N * 2
+                print(json.dumps({
+                    "sweep": "config2", "M": M, "K": K, "N": N, "us_graph": round(ug, 2),
+                    "us_eager": round(ue, 2), "GBs_graph": round(nb / ug / 1e3, 1),
+                    "frac_hbm_graph": round(nb / ug / 1e3 / hbm, 3),
+                    "cublas_fp16_us_graph": round(cg_, 2), "cublas_fp16_us_eager": round(ce, 2),
+                    "speedup_vs_cublas_graph": round(cg_ / ug, 2),
+                    "speedup_vs_cublas_eager": round(ce / ue, 2),
+                    "byte_ratio_ceiling": round(b16 / nb, 3), "peak_source": src}), flush=True)
+        else:
+            for M in SWEEP3_M:
+                for dt in (torch.float16, torch.bfloat16):
+                    X = torch.randn(M, K, generator=torch.Generator().manual_seed(M)).to(dt).cuda()
+                    Y = torch.empty(M, N, dtype=dt, device="cuda")
+                    ours = lambda i: ext.gemm_w4a16(X, Q[i % nrot], S, 128, out=Y)
+                    Wd = W16s if dt == torch.float16 else [w.to(dt) for w in W16s]
+                    Yc = torch.empty(M, N, dtype=dt, device="cuda")
+                    cub = lambda i: torch.mm(X, Wd[i % len(Wd)], out=Yc)
+                    flops = 2.0 * M * K * N
+                    n = max(5, min(100, int(2e12 / flops)))
+                    ug, cg_ = _graph_us(ours, n, stream), _graph_us(cub, n, stream)
+                    print(json.dumps({
+                        "sweep": "config3", "M": M, "K": K, "N": N, "dtype": str(dt).split(".")[-1],
+                        "us_graph": round(ug, 2), "TFLOPs": round(flops / ug / 1e6, 1),
+                        "frac_dense_peak": round(flops / ug / 1e6 / bf16_peak, 3),
+                        "GBs": round(algo_bytes(M, K, N, 128) / ug / 1e3, 1),
+                        "cublas_dense_us_graph": round(cg_, 2),
+                        "cublas_dense_TFLOPs": round(flops / cg_ / 1e6, 1),
+                        "peak_source": src}), flush=True)
+                    del Wd
+        del Q, W16s, W16
+        torch.cuda.empty_cache()
+    assert ext.device_status() == 0, "a kernel reported a bounded-wait timeout"
 
 
 def algo_bytes(M, K, N, G):
@@ -305,6 +412,10 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.workload == "step8b":
         return run_step(args, wl, world, rank, local, dist)
+    if args.workload in ("sweep2", "sweep3"):
+        if rank == 0:
+            run_sweep(args, local)
+        return
     M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
     from oracle import quant_oracle as qo  # seeded synthetic inputs (generator only)
     x, q, s = qo.synthetic_case(M, K, N, group_size=G, seed=1 + rank)
