@@ -97,11 +97,12 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     order; block_threads 0 (256), 128 or 256;  algo 1 = fp16 decode with
  *     packed-half2 FMA windows of 32 values flushed to fp32 (fp16 x only),
  *     algo 2 = fp32 decode with packed fp32x2 FMA (the default for bf16 x).
- *   - algo 0 (default), with block_threads == 0 and splits <= 8, M <= 8:
- *     algo 5 with one K slice per column tile when N >= 12288 and (M >= 2 or
- *     K <= 4096); algo 5 (stream-K) when M is 3..4 and the packed weight is
+ *   - algo 0 (default), with block_threads == 0 and splits <= 8:
+ *     algo 5 with one K slice per column tile when N >= 12288, M <= 8 and
+ *     (M >= 2 or K <= 4096); algo 5 (stream-K) when M is 3..4 and the packed weight is
  *     >= 12 MiB; algo 5 when M > 4; otherwise algo 1 (fp16 x) / 2 (bf16 x).
- *   - bulk-copy ring (algo 4 / 5; M <= 8; the workspace only for stream-K):
+ *   - bulk-copy ring (algo 4: M <= 8, algo 5: M <= 16; the workspace only for
+ *     stream-K):
  *     one producer warp per CTA streams the CTA's (128-column, K-slice) weight
  *     block into a shared-memory ring with 2-D TMA loads, consumer warps
  *     decode from shared memory -- algo 4 with the algo 1 (fp16 x) / algo 2
@@ -159,9 +160,20 @@ int ng_gemv_w4a16_noalloc(const void* x, int x_dtype, const int32_t* qweight,
  *   Any M >= 1; K % 64 == 0; N % 4 == 0; group_size in {64, 128, 256};
  *   x, qweight 16-byte aligned; scales 2-byte aligned.
  *   tile_tokens: 0 = heuristic, else 16, 32, 64, 128 or 256 rows of X per tile.
+ *   workspace (may be NULL): ng_gemm_workspace_bytes(M, N) bytes, 256-byte
+ *   aligned, zero-filled before first use.  With it, grids that would leave
+ *   SMs idle (few tiles: small M, or N = 4096 with long K) are split along K;
+ *   each split writes fp32 partials there and the last split of a tile to
+ *   finish sums them in split order (deterministic) and re-arms the tile's
+ *   counter, so the workspace is reusable as is.  Without it, no K split.
+ *   Calls sharing a workspace must not overlap on the GPU.
  */
 int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
-                  void* y, int M, int K, int N, int group_size, int tile_tokens, void* stream);
+                  void* y, int M, int K, int N, int group_size, int tile_tokens, void* workspace,
+                  size_t workspace_bytes, void* stream);
+/* Workspace bytes ng_gemm_w4a16 can use for an [M, N] output on the current
+ * device (0 if M or N is out of range). */
+size_t ng_gemm_workspace_bytes(int M, int N);
 
 /*
  * Tensor-parallel reduction for the decode step: one-shot all-reduce (sum) of

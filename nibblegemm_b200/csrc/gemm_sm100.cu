@@ -60,13 +60,15 @@ struct Barriers {
   uint64_t tempty[2];
   uint32_t tmem_slot;
   int abort;
+  int last;  // split-K: this CTA's epilogue finishes the current tile
 };
 
 template <int BT, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ CUtensorMap tmap_q, const __half* __restrict__ scales,
-                void* __restrict__ y, int M, int K, int N, int G, int stages,
+                void* __restrict__ y, int M, int K, int N, int G, int stages, int splits,
+                float* __restrict__ ws_part, unsigned int* __restrict__ ws_cnt,
                 unsigned int* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzled operand tiles.
@@ -83,6 +85,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m_tiles = (M + BT - 1) / BT;
   const int tiles = n_tiles * m_tiles;
   const int kb_count = K / kBK;
+  // Work units: (tile, K split); unit u covers k-steps [kbs * (u % splits), + kbs).
+  const int units = tiles * splits;
+  const int kbs = kb_count / splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -109,10 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+        const int tile = u / splits, kb0 = (u % splits) * kbs;
         const int n0 = (tile % n_tiles) * kTileN;
         const int m0 = (tile / n_tiles) * BT;
-        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+        for (int kb = kb0; kb < kb0 + kbs; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t ph = (it / stages) & 1;
           if (!mbar_wait_bounded(&bars->empty[s], ph ^ 1, err, abort)) break;
@@ -128,14 +134,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(BF16, kTileN, BT);
       int it = 0, lt = 0;
-      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, ++lt) {
+      for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++lt) {
         const int acc = lt & 1;
         const uint32_t aph = (lt >> 1) & 1;
         if (!mbar_wait_bounded(&bars->tempty[acc], aph ^ 1, err, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BT;
         bool ok = true;
-        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+        for (int kb = 0; kb < kbs; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t ph = (it / stages) & 1;
           if (!mbar_wait_bounded(&bars->full[s], ph, err, abort) ||
@@ -165,7 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int e = warp - 4;  // TMEM lanes 32e .. 32e+31
     int lt = 0;
     unsigned short* yo = static_cast<unsigned short*>(y);
-    for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x, ++lt) {
+    for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x, ++lt) {
+      const int tile = u / splits;
       const int n0 = (tile % n_tiles) * kTileN;
       const int m0 = (tile / n_tiles) * BT;
       const int acc = lt & 1;
@@ -179,7 +186,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[16];
         tmem_ld_16(taddr + c0, r);
         tmem_ld_wait();
-        if (n < N) {
+        if (splits > 1) {  // fp32 partial of this unit, [BT][128] (coalesced over n)
+          float* part = ws_part + static_cast<size_t>(u) * BT * kTileN;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) part[(c0 + j) * kTileN + e * 32 + lane] = __uint_as_float(r[j]);
+        } else if (n < N) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c0 + j;
@@ -194,24 +205,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+      if (splits > 1) {
+        // Last unit of the tile to arrive sums the partials in split order
+        // (deterministic), writes Y, and re-arms the tile's counter.
+        __threadfence();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (warp == 4 && lane == 0)
+          bars->last = atomicAdd(&ws_cnt[tile], 1u) == static_cast<unsigned int>(splits - 1);
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (bars->last) {
+          __threadfence();
+          const float* base = ws_part + static_cast<size_t>(tile) * splits * BT * kTileN;
+          for (int m = 0; m < BT && m0 + m < M; ++m) {
+            float v = 0.f;
+            for (int sp = 0; sp < splits; ++sp)
+              v += __ldcg(base + (static_cast<size_t>(sp) * BT + m) * kTileN + e * 32 + lane);
+            if (n < N)
+              yo[static_cast<size_t>(m0 + m) * N + n] = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                             : __half_as_ushort(__float2half_rn(v));
+          }
+          if (warp == 4 && lane == 0) ws_cnt[tile] = 0u;
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      }
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ dequant
     const int t = (threadIdx.x - 256) & (kTileN - 1);  // weight column within the tile
     const int grp = (threadIdx.x - 256) >> 7;            // this group decodes k-steps it % kDequantGroups == grp
     const int atom = t >> 3, r8 = t & 7;
-    const int my_tiles = tiles > static_cast<int>(blockIdx.x)
-                             ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+    const int my_units = units > static_cast<int>(blockIdx.x)
+                             ? (units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
                              : 0;
-    const int total = my_tiles * kb_count;
+    const int total = my_units * kbs;
     // Scale of iteration i (flattened over this CTA's tiles x k-steps); loaded
     // kPrefetch iterations ahead so its global-memory latency never sits
     // between a stage landing and its decode.
     auto scale_at = [&](int i) -> __half {
       if (i >= total) return __float2half(0.f);
-      const int tile = static_cast<int>(blockIdx.x) + (i / kb_count) * static_cast<int>(gridDim.x);
+      const int u = static_cast<int>(blockIdx.x) + (i / kbs) * static_cast<int>(gridDim.x);
+      const int tile = u / splits;
       const int n = (tile % n_tiles) * kTileN + t;
-      const int g = ((i % kb_count) * kBK) / G;
+      const int g = (((u % splits) * kbs + i % kbs) * kBK) / G;
       return n < N ? scales[static_cast<size_t>(g) * N + n] : __float2half(0.f);
     };
     constexpr int kPrefetch = 4;
@@ -316,9 +351,24 @@ int make_maps(const void* x, const int32_t* q, int M, int K, int N, int BT, CUte
   return NG_OK;
 }
 
+// K splits for grids that would leave SMs idle: the largest divisor d of the
+// k-step count with tiles * d <= SMs, d <= 16 and >= 8 k-steps per unit
+// (1 without a large enough workspace).
+int pick_splits(int tiles, int kb_count, int sm_count) {
+  int best = 1;
+  for (int d = 2; d <= 16; ++d)
+    if (kb_count % d == 0 && kb_count / d >= 8 && tiles * d <= sm_count) best = d;
+  return best;
+}
+
+size_t gemm_ws_bytes(int tiles, int splits, int BT) {
+  return splits > 1 ? static_cast<size_t>(tiles) * splits * BT * kTileN * 4 + static_cast<size_t>(tiles) * 4
+                    : 0;
+}
+
 template <int BT, bool BF16>
 int run_gemm(const void* x, const int32_t* q, const __half* s, void* y, int M, int K, int N, int G,
-             const DeviceInfo& dev, cudaStream_t stream) {
+             void* ws, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
   CUtensorMap mx, mq;
   if (int st = make_maps(x, q, M, K, N, BT, &mx, &mq)) return st;
   constexpr int stage_bytes = kATileBytes + BT * kBK * 2 + kRawBytes;
@@ -330,20 +380,27 @@ int run_gemm(const void* x, const int32_t* q, const __half* s, void* y, int M, i
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 4096);
   });
   const int tiles = ((N + kTileN - 1) / kTileN) * ((M + BT - 1) / BT);
-  const int grid = std::min(tiles, dev.sm_count);
-  kern<<<grid, kThreads, smem, stream>>>(mx, mq, s, y, M, K, N, G, stages, dev.err);
+  int splits = pick_splits(tiles, K / kBK, dev.sm_count);
+  if (ws == nullptr || ws_bytes < gemm_ws_bytes(tiles, splits, BT)) splits = 1;
+  float* ws_part = static_cast<float*>(ws);
+  unsigned int* ws_cnt = splits > 1 ? reinterpret_cast<unsigned int*>(
+                                          ws_part + static_cast<size_t>(tiles) * splits * BT * kTileN)
+                                    : nullptr;
+  const int grid = std::min(tiles * splits, dev.sm_count);
+  kern<<<grid, kThreads, smem, stream>>>(mx, mq, s, y, M, K, N, G, stages, splits, ws_part, ws_cnt,
+                                         dev.err);
   return launch_status();
 }
 
 template <bool BF16>
 int dispatch_bt(int bt, const void* x, const int32_t* q, const __half* s, void* y, int M, int K,
-                int N, int G, const DeviceInfo& dev, cudaStream_t st) {
+                int N, int G, void* ws, size_t wsb, const DeviceInfo& dev, cudaStream_t st) {
   switch (bt) {
-    case 16: return run_gemm<16, BF16>(x, q, s, y, M, K, N, G, dev, st);
-    case 32: return run_gemm<32, BF16>(x, q, s, y, M, K, N, G, dev, st);
-    case 64: return run_gemm<64, BF16>(x, q, s, y, M, K, N, G, dev, st);
-    case 128: return run_gemm<128, BF16>(x, q, s, y, M, K, N, G, dev, st);
-    default: return run_gemm<256, BF16>(x, q, s, y, M, K, N, G, dev, st);
+    case 16: return run_gemm<16, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    case 32: return run_gemm<32, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    case 64: return run_gemm<64, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    case 128: return run_gemm<128, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    default: return run_gemm<256, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
   }
 }
 
@@ -366,9 +423,19 @@ int pick_bt(int M, int N, int sm_count) {
 }  // namespace
 }  // namespace ngb
 
+extern "C" size_t ng_gemm_workspace_bytes(int M, int N) {
+  using namespace ngb;
+  DeviceInfo dev;
+  if (M < 1 || N <= 0 || current_device_info(&dev) != NG_OK) return 0;
+  // split-K is used only while units = tiles x splits <= SMs
+  const int bt = pick_bt(M, N, dev.sm_count);
+  return static_cast<size_t>(dev.sm_count) * (static_cast<size_t>(bt) * kTileN * 4 + 4);
+}
+
 extern "C" int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight,
                              const uint16_t* scales, void* y, int M, int K, int N, int group_size,
-                             int tile_tokens, void* stream) {
+                             int tile_tokens, void* workspace, size_t workspace_bytes,
+                             void* stream) {
   using namespace ngb;
   if (!x || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
   if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
@@ -379,7 +446,8 @@ extern "C" int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   if (tile_tokens != 0 && tile_tokens != 16 && tile_tokens != 32 && tile_tokens != 64 &&
       tile_tokens != 128 && tile_tokens != 256)
     return NG_ERR_BAD_ARGUMENT;
-  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 2) || !aligned(y, 2))
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 2) || !aligned(y, 2) ||
+      !aligned(workspace, 256))
     return NG_ERR_MISALIGNED;
   DeviceInfo dev;
   if (int st = current_device_info(&dev)) return st;
@@ -387,6 +455,8 @@ extern "C" int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   auto* s = reinterpret_cast<const __half*>(scales);
   auto strm = static_cast<cudaStream_t>(stream);
   if (x_dtype == NG_DTYPE_BF16)
-    return dispatch_bt<true>(bt, x, qweight, s, y, M, K, N, group_size, dev, strm);
-  return dispatch_bt<false>(bt, x, qweight, s, y, M, K, N, group_size, dev, strm);
+    return dispatch_bt<true>(bt, x, qweight, s, y, M, K, N, group_size, workspace, workspace_bytes,
+                             dev, strm);
+  return dispatch_bt<false>(bt, x, qweight, s, y, M, K, N, group_size, workspace, workspace_bytes,
+                            dev, strm);
 }

@@ -400,7 +400,7 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
   if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
   if (algo < 0 || algo > 5) return NG_ERR_BAD_ARGUMENT;
-  if (algo >= 4 && (M > 8 || splits > 8)) return NG_ERR_BAD_ARGUMENT;
+  if (algo >= 4 && (M > (algo == 5 ? 16 : 8) || splits > 8)) return NG_ERR_BAD_ARGUMENT;
   if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
   if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2) ||
       !aligned(workspace, 256))
@@ -420,18 +420,18 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
     }
   }
   // Default schedule (measured on B200, M <= 8, no cluster-kernel options):
-  //   * >= 96 column tiles (N >= 12288) and M >= 2 or K <= 4096: the ring with
+  //   * >= 96 column tiles (N >= 12288), M <= 8 and M >= 2 or K <= 4096: the ring with
   //     one CTA per tile (its CTAs sweep the rows in lockstep);
   //   * M = 3..4 and a packed weight >= 12 MiB: the stream-K ring (all SMs);
-  //   * M > 4: the ring with its own K split;
+  //   * M > 4 (up to 16): the ring with its own K split;
   //   * otherwise the cluster kernel.
-  if (algo == 0 && M <= 8 && block_threads == 0 && splits <= 8) {
+  if (algo == 0 && block_threads == 0 && splits <= 8) {
     const int tiles = (N + 127) / 128;
     const double wbytes = static_cast<double>(K) * N / 2.0;
-    if (tiles >= 96 && (M > 1 || K <= 4096)) {
+    if (tiles >= 96 && M <= 8 && (M > 1 || K <= 4096)) {
       algo = 5;
       if (splits == 0) splits = 1;
-    } else if (M > 4 || (M >= 3 && wbytes >= 12.0 * (1 << 20))) {
+    } else if (M > 4 || (M >= 3 && wbytes >= 12.0 * (1 << 20))) {  // includes M = 9..16
       algo = 5;
     }
   }

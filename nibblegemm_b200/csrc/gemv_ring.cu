@@ -291,15 +291,21 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
       const int g = lane >> 2, t = lane & 3;
       constexpr uint32_t kC0 = XBF16 ? 0x43084308u : 0x64086408u;  // 136 (bf16) / 1032 (fp16)
       constexpr uint32_t kC1 = XBF16 ? 0x43084308u : 0x64806480u;  // 136 (bf16) / 1152 (fp16)
-      float tot[2][4][4], c[2][4][4], cv[4];
+      // NT tiles of 8 tokens (MMA N = 8): tokens 8 nt + g feed the B fragment
+      constexpr int NT = (MT + 7) / 8;
+      float tot[2][4][NT][4], c[2][4][NT][4], cv[NT][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) tot[h][i][r] = c[h][i][r] = 0.f;
+          for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+            for (int r = 0; r < 4; ++r) tot[h][i][nt][r] = c[h][i][nt][r] = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) cv[nt][r] = 0.f;
       for (int s = 0; s < nst; ++s) {
         const int slot = s % stages;
         if (!mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) break;
@@ -319,8 +325,13 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
             w[2 * h + 1] = *reinterpret_cast<const uint4*>(src + (64 * h + 32 + 4 * g) * 4);
           }
           const int lrow = s * Cfg::kStageRows + row;  // slice-local packed row of the step
-          uint4 xv = make_uint4(0u, 0u, 0u, 0u);
-          if (g < MT) xv = *reinterpret_cast<const uint4*>(xs + g * xstride + (lrow + t) * 8);
+          uint4 xv[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            xv[nt] = make_uint4(0u, 0u, 0u, 0u);
+            if (8 * nt + g < MT)
+              xv[nt] = *reinterpret_cast<const uint4*>(xs + (8 * nt + g) * xstride + (lrow + t) * 8);
+          }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t wa[4] = {w[2 * h].x, w[2 * h].y, w[2 * h].z, w[2 * h].w};
@@ -330,12 +341,18 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
               uint32_t ha[4], hb[4];
               decode_mma_operands<XBF16>(wa[i], ha);
               decode_mma_operands<XBF16>(wb[i], hb);
-              ring_mma<XBF16>(c[h][i], ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
-              ring_mma<XBF16>(c[h][i], ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                ring_mma<XBF16>(c[h][i][nt], ha[0], hb[0], ha[1], hb[1], xv[nt].x, xv[nt].y);
+                ring_mma<XBF16>(c[h][i][nt], ha[2], hb[2], ha[3], hb[3], xv[nt].z, xv[nt].w);
+              }
             }
           }
-          ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.x, xv.y);
-          ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.z, xv.w);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            ring_mma<XBF16>(cv[nt], kC0, kC0, kC1, kC1, xv[nt].x, xv[nt].y);
+            ring_mma<XBF16>(cv[nt], kC0, kC0, kC1, kC1, xv[nt].z, xv[nt].w);
+          }
           // flush at the end of a quantisation group or of this warp's rows
           const int gnext = kr0 + lrow + 4;
           if ((gnext * 8) % G == 0 || row + 4 >= rend) {
@@ -352,14 +369,18 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                  if (MT == 1 && (r & 1)) continue;  // token 2t + 1 >= 1: nothing to keep
-                  tot[h][i][r] = fmaf(r < 2 ? fa[i] : fb[i], c[h][i][r] - cv[r & 1], tot[h][i][r]);
-                  c[h][i][r] = 0.f;
-                }
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                  for (int r = 0; r < 4; ++r) {
+                    if (MT == 1 && (r & 1)) continue;  // token 2t + 1 >= 1: nothing to keep
+                    tot[h][i][nt][r] = fmaf(r < 2 ? fa[i] : fb[i], c[h][i][nt][r] - cv[nt][r & 1], tot[h][i][nt][r]);
+                    c[h][i][nt][r] = 0.f;
+                  }
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int r = 0; r < 4; ++r) cv[nt][r] = 0.f;
           }
         }
         __syncwarp();
@@ -371,11 +392,13 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int m = 2 * t + (r & 1);
-            const int col = 64 * h + (r < 2 ? 0 : 32) + 4 * g + i;
-            if (m < MT) red[(warp * MT + m) * kRCols + col] = tot[h][i][r];
-          }
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const int m = 8 * nt + 2 * t + (r & 1);
+              const int col = 64 * h + (r < 2 ? 0 : 32) + 4 * g + i;
+              if (m < MT) red[(warp * MT + m) * kRCols + col] = tot[h][i][nt][r];
+            }
     } else {
       for (int s = 0; s < nst; ++s) {
         const int slot = s % stages;
@@ -862,6 +885,8 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   } else {
     for (int c : {2, 4})
       if (tiles * c <= sms && krows / c >= 128) C = c;
+    // keep the staged activations of the slice within 64 KB (M = 9..16)
+    while (C < kMaxRingCluster && static_cast<long>(MT) * (krows / C) * 8 * esz > 64 * 1024) C *= 2;
   }
   C = std::max(1, std::min(C, std::min(kMaxRingCluster, krows / 8)));
   int rows_per_cta = (((krows + C - 1) / C) + 7) / 8 * 8;
@@ -913,7 +938,8 @@ int ring_dispatch_m(const void* x, const uint32_t* qw, const __half* s, void* y,
   if (M <= 1) return run_ring<1, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
   if (M <= 2) return run_ring<2, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
   if (M <= 4) return run_ring<4, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  return run_ring<8, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  if (M <= 8 || PATH != kRMma) return run_ring<8, XBF16, PATH, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
+  return run_ring<16, XBF16, kRMma, RW>(x, qw, s, y, M, K, N, G, splits, dev, st);
 }
 
 // Tensor-pipe consumer: packed rows per warp per stage (16 = fewest flushes,
@@ -1015,7 +1041,7 @@ size_t gemv_ring_workspace_bytes(int N, const DeviceInfo& dev) {
 int gemv_ring(const void* x, int x_dtype, bool tensor_pipe, const uint32_t* q, const __half* s,
               void* y, int M, int K, int N, int G, int splits, void* ws, size_t ws_bytes,
               const DeviceInfo& dev, cudaStream_t strm) {
-  if (M > 8 || splits > kMaxRingCluster) return NG_ERR_BAD_ARGUMENT;
+  if (M > (tensor_pipe ? 16 : 8) || splits > kMaxRingCluster) return NG_ERR_BAD_ARGUMENT;
   // Stream-K over all SMs when it applies (tensor pipe, M <= 4, X on chip, a
   // workspace, no explicit split); the clustered K split otherwise.
   if (tensor_pipe && splits == 0 && M <= kSkMaxM) {

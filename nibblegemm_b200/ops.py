@@ -78,6 +78,18 @@ class _Extension:
     def __init__(self):
         self.lib = _lib.load()
         self._ws = {}  # (device index, stream handle) -> zero-initialised GEMV workspace
+        self._gws = {}  # (device index, stream handle) -> zero-initialised GEMM split-K workspace
+
+    def gemm_workspace(self, M: int, N: int, device: torch.device, stream: int) -> torch.Tensor:
+        """The prefill-GEMM split-K workspace for (device, stream), grown on demand
+        (zero-filled once; every call leaves its per-tile counters at zero)."""
+        need = self.lib.ng_gemm_workspace_bytes(M, N)
+        key = (device.index, stream)
+        ws = self._gws.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+            self._gws[key] = ws
+        return ws
 
     def workspace(self, N: int, device: torch.device, stream: int) -> torch.Tensor:
         """The decode-GEMV workspace for (device, stream), grown on demand.
@@ -137,9 +149,11 @@ class _Extension:
         _require(version in (6, 7), "version must be 6 or 7")
         y = _out(out, M, N, X)
         with _on_device(X.device):
+            stream = torch.cuda.current_stream().cuda_stream
+            ws = self.gemm_workspace(M, N, X.device, stream)
             st = self.lib.ng_gemm_w4a16(X.data_ptr(), _DTYPE_CODE[X.dtype], Wq.data_ptr(),
                                         S.data_ptr(), y.data_ptr(), M, K, N, int(group_size),
-                                        int(tile_tokens), torch.cuda.current_stream().cuda_stream)
+                                        int(tile_tokens), ws.data_ptr(), ws.numel(), stream)
         _lib.check(st, "gemm_w4a16")
         return y
 

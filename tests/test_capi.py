@@ -37,7 +37,7 @@ def status_codes():
 
 def test_library_builds_and_loads():
     lib = _lib.load()
-    assert lib.ng_abi_version() == 1
+    assert lib.ng_abi_version() == 2
 
 
 def test_every_declared_symbol_is_exported_and_bound():
@@ -65,7 +65,7 @@ def test_null_pointers_rejected():
     lib = _lib.load()
     c = status_codes()
     assert lib.ng_gemv_w4a16(None, 0, FAKE, FAKE, FAKE, 1, 256, 128, 128, 0, 0, 0, None, 0, None) == c["NG_ERR_NULL_POINTER"]
-    assert lib.ng_gemm_w4a16(FAKE, 0, None, FAKE, FAKE, 32, 256, 128, 128, 0, None) == c["NG_ERR_NULL_POINTER"]
+    assert lib.ng_gemm_w4a16(FAKE, 0, None, FAKE, FAKE, 32, 256, 128, 128, 0, None, 0, None) == c["NG_ERR_NULL_POINTER"]
     assert lib.ng_dequant_w4(FAKE, None, FAKE, 0, 256, 128, 128, 1, None) == c["NG_ERR_NULL_POINTER"]
 
 

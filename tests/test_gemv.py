@@ -263,3 +263,15 @@ def test_ring_stream_k_matches_oracle_and_leaves_flags_zero(M, K, N, G, act):
     total = ext.lib.ng_gemv_workspace_bytes(1, N)
     sm = torch.cuda.get_device_properties(X.device).multi_processor_count
     assert int(ws[total - 4 * sm: total].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(9, 1024, 388), (12, 4096, 1028), (16, 4096, 14336), (16, 14336, 4096),
+                                   (13, 2048, 132), (16, 8192, 8192)])
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+def test_ring_tensor_pipe_two_token_tiles(M, K, N, act):
+    """algo 5 at M = 9..16 (two 8-token MMA tiles), and the default schedule
+    that routes there."""
+    X, qw, ref = make_case(M, K, N, 128, seed=M * 3 + N, act=act)
+    check(ng.gemv(X, qw, algo=5), ref, X.dtype)
+    check(ng.gemv(X, qw), ref, X.dtype)
+    assert ng.extension().device_status() == 0
