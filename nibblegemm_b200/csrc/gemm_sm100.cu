@@ -361,8 +361,13 @@ int pick_splits(int tiles, int kb_count, int sm_count) {
   return best;
 }
 
-size_t gemm_ws_bytes(int tiles, int splits, int BT) {
-  return splits > 1 ? static_cast<size_t>(tiles) * splits * BT * kTileN * 4 + static_cast<size_t>(tiles) * 4
+// Workspace layout: per-tile arrival counters at a fixed offset (a split grid
+// has at most SMs / 2 tiles), then the fp32 partials.  The counters' place must
+// not depend on the call's shape: a later call must find them where an
+// earlier call of any shape left them (at zero).
+size_t gemm_ws_counter_bytes(int sm_count) { return (static_cast<size_t>(sm_count) * 4 + 255) / 256 * 256; }
+size_t gemm_ws_bytes(int tiles, int splits, int BT, int sm_count) {
+  return splits > 1 ? gemm_ws_counter_bytes(sm_count) + static_cast<size_t>(tiles) * splits * BT * kTileN * 4
                     : 0;
 }
 
@@ -381,11 +386,11 @@ int run_gemm(const void* x, const int32_t* q, const __half* s, void* y, int M, i
   });
   const int tiles = ((N + kTileN - 1) / kTileN) * ((M + BT - 1) / BT);
   int splits = pick_splits(tiles, K / kBK, dev.sm_count);
-  if (ws == nullptr || ws_bytes < gemm_ws_bytes(tiles, splits, BT)) splits = 1;
-  float* ws_part = static_cast<float*>(ws);
-  unsigned int* ws_cnt = splits > 1 ? reinterpret_cast<unsigned int*>(
-                                          ws_part + static_cast<size_t>(tiles) * splits * BT * kTileN)
-                                    : nullptr;
+  if (ws == nullptr || ws_bytes < gemm_ws_bytes(tiles, splits, BT, dev.sm_count)) splits = 1;
+  unsigned int* ws_cnt = splits > 1 ? static_cast<unsigned int*>(ws) : nullptr;
+  float* ws_part = splits > 1 ? reinterpret_cast<float*>(static_cast<unsigned char*>(ws) +
+                                                         gemm_ws_counter_bytes(dev.sm_count))
+                              : nullptr;
   const int grid = std::min(tiles * splits, dev.sm_count);
   kern<<<grid, kThreads, smem, stream>>>(mx, mq, s, y, M, K, N, G, stages, splits, ws_part, ws_cnt,
                                          dev.err);
@@ -429,7 +434,7 @@ extern "C" size_t ng_gemm_workspace_bytes(int M, int N) {
   if (M < 1 || N <= 0 || current_device_info(&dev) != NG_OK) return 0;
   // split-K is used only while units = tiles x splits <= SMs
   const int bt = pick_bt(M, N, dev.sm_count);
-  return static_cast<size_t>(dev.sm_count) * (static_cast<size_t>(bt) * kTileN * 4 + 4);
+  return gemm_ws_counter_bytes(dev.sm_count) + static_cast<size_t>(dev.sm_count) * bt * kTileN * 4;
 }
 
 extern "C" int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight,

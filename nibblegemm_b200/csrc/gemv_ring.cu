@@ -885,9 +885,11 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   } else {
     for (int c : {2, 4})
       if (tiles * c <= sms && krows / c >= 128) C = c;
-    // keep the staged activations of the slice within 64 KB (M = 9..16)
-    while (C < kMaxRingCluster && static_cast<long>(MT) * (krows / C) * 8 * esz > 64 * 1024) C *= 2;
   }
+  // Keep the staged activations of a slice within 64 KB (M = 9..16): the split
+  // count is raised if needed (a request, not a promise, as for the cluster GEMV).
+  while (C < kMaxRingCluster && static_cast<long>(MT) * ((krows + C - 1) / C) * 8 * esz > 64 * 1024)
+    C = std::min(kMaxRingCluster, C * 2);
   C = std::max(1, std::min(C, std::min(kMaxRingCluster, krows / 8)));
   int rows_per_cta = (((krows + C - 1) / C) + 7) / 8 * 8;
   C = (krows + rows_per_cta - 1) / rows_per_cta;

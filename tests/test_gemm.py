@@ -140,5 +140,23 @@ def test_split_k_matches_oracle_deterministic_and_reusable(M, K, N, act):
                                torch.cuda.current_stream().cuda_stream)
     assert st == 0
     d = (y.float() - y1.float()).abs().max().item() / y1.float().abs().max().item()
-    assert d < 4e-3
+    assert d < (1e-2 if act == "bf16" else 2e-3)  # ~two output ulps: only the fp32 summation order differs
     assert ext.device_status() == 0
+
+
+def test_split_k_workspace_shared_across_shapes():
+    """One workspace serves calls of different shapes in any order (the
+    counters sit at a fixed place, partials never overlap them)."""
+    ext = ng.extension()
+    cases = [make_case(M, K, N, 128, seed=i, act=act) for i, (M, K, N, act) in
+             enumerate([(300, 1024, 392, "bf16"), (16, 14336, 4096, "f16"), (40, 8192, 2048, "bf16"),
+                        (128, 4096, 1024, "f16")])]
+    first = [ext.gemm_w4a16(X, qw.qweight, qw.scales, 128, tile_tokens=32) for _, _, _, X, qw in cases]
+    for _ in range(2):
+        for (x, q, s, X, qw), y0 in zip(reversed(cases), reversed(first)):
+            assert torch.equal(y0, ext.gemm_w4a16(X, qw.qweight, qw.scales, 128, tile_tokens=32))
+    for (x, q, s, X, qw), y in zip(cases, first):
+        M, K = X.shape
+        rows = np.unique(np.linspace(0, M - 1, num=min(M, 8)).astype(int))
+        act = "bf16" if X.dtype == torch.bfloat16 else "f16"
+        check(y[torch.from_numpy(rows).cuda()], oracle(x, q, s, 128, K, act, rows), X.dtype)
