@@ -56,10 +56,22 @@ constexpr int kMaxRingCluster = 8;
 // stage), or mma.sync on magic-number operands (16 rows per warp per stage).
 enum RPath { kRHalf2 = 0, kRFloat2 = 1, kRMma = 2 };
 
-template <int CW, int PATH, int RW>
+// Stage geometry: SR packed rows per stage.  SR = CW x RW: every consumer warp
+// takes RW rows of every stage.  SR < CW x RW: a stage is taken by SR / RW
+// warps and the warp groups take consecutive stages round-robin (smaller
+// stages, released as soon as their few warps are done).  Measured on B200:
+// whole-CTA 64 KB stages are faster up to M = 8 (config 1: 9.3 us vs 11.0 us
+// with 16 KB stages), 16 KB stages at M = 9..16, where the staged activations
+// leave room for only a few large stages (14336 x 4096: 26 us vs 52 us).
+template <int MT, int PATH>
+constexpr int ring_stage_rows(int CW, int RW) { return (PATH == kRMma && MT > 8) ? 32 : CW * RW; }
+
+template <int CW, int PATH, int RW, int SR = CW * RW>
 struct RingCfg {
   static constexpr int kRowsPerWarp = RW;
-  static constexpr int kStageRows = CW * kRowsPerWarp;
+  static constexpr int kStageRows = SR;
+  static constexpr int kWarpsPerStage = kStageRows / RW;
+  static constexpr int kStageGroups = CW / kWarpsPerStage;
   static constexpr int kStageBytes = kStageRows * kRCols * 4;
   static constexpr int kThreads = (CW + 1) * 32;  // + one producer warp
 };
@@ -158,11 +170,11 @@ __device__ __forceinline__ void decode_mma_operands(uint32_t q, uint32_t (&h)[4]
 }
 
 template <int MT, bool XBF16, int PATH, int CW, int RW>
-__global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
+__global__ void __launch_bounds__(RingCfg<CW, PATH, RW, ring_stage_rows<MT, PATH>(CW, RW)>::kThreads, 1)
     gemv_ring_kernel(const __grid_constant__ CUtensorMap tmap_q, const void* __restrict__ x,
                      const __half* __restrict__ scales, void* __restrict__ y, int M, int K, int N,
                      int G, int rows_per_cta, int csize, int stages, unsigned int* __restrict__ err) {
-  using Cfg = RingCfg<CW, PATH, RW>;
+  using Cfg = RingCfg<CW, PATH, RW, ring_stage_rows<MT, PATH>(CW, RW)>;
   constexpr int kRowsPerWarp = Cfg::kRowsPerWarp;
   using XS = typename std::conditional<PATH == kRFloat2, float, __half>::type;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -181,6 +193,10 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
   const int c0 = blockIdx.x * kRCols;
   const int g0 = (kr0 * 8) / G;
   const int ngroups = nrows > 0 ? (kr1 * 8 - 1) / G - g0 + 1 : 0;
+  if (nst > stages && stages % Cfg::kStageGroups != 0) {  // host guarantees this; never wait ambiguously
+    if (threadIdx.x == 0) atomicOr(err, kErrWaitTimeout);
+    return;
+  }
   const RingLayout L(stages, Cfg::kStageBytes, MT, rows_per_cta, sizeof(XS),
                      rows_per_cta * 8 / G + 2, CW);
   unsigned char* ring = smem + L.ring;
@@ -193,7 +209,7 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CW);
+      mbar_init(&empty[i], Cfg::kWarpsPerStage);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -306,11 +322,11 @@ __global__ void __launch_bounds__(RingCfg<CW, PATH, RW>::kThreads, 1)
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int r = 0; r < 4; ++r) cv[nt][r] = 0.f;
-      for (int s = 0; s < nst; ++s) {
+      for (int s = warp / Cfg::kWarpsPerStage; s < nst; s += Cfg::kStageGroups) {
         const int slot = s % stages;
         if (!mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) break;
         const int rows_here = min(Cfg::kStageRows, nrows - s * Cfg::kStageRows);
-        const int rr0 = warp * kRowsPerWarp;
+        const int rr0 = (warp % Cfg::kWarpsPerStage) * kRowsPerWarp;
         const int rend = min(rr0 + kRowsPerWarp, rows_here);
         const unsigned char* stage_base = ring + static_cast<size_t>(slot) * Cfg::kStageBytes;
 #pragma unroll
@@ -858,7 +874,7 @@ constexpr int kCW = 8;
 template <int MT, bool XBF16, int PATH, int RW>
 int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N, int G,
              int splits, const DeviceInfo& dev, cudaStream_t stream) {
-  using Cfg = RingCfg<kCW, PATH, RW>;
+  using Cfg = RingCfg<kCW, PATH, RW, ring_stage_rows<MT, PATH>(kCW, RW)>;
   auto kern = gemv_ring_kernel<MT, XBF16, PATH, kCW, RW>;
   constexpr int esz = PATH == kRFloat2 ? 4 : 2;
   const int krows = K / 8;
@@ -886,9 +902,13 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
     for (int c : {2, 4})
       if (tiles * c <= sms && krows / c >= 128) C = c;
   }
-  // Keep the staged activations of a slice within 64 KB (M = 9..16): the split
-  // count is raised if needed (a request, not a promise, as for the cluster GEMV).
-  while (C < kMaxRingCluster && static_cast<long>(MT) * ((krows + C - 1) / C) * 8 * esz > 64 * 1024)
+  // The slice's staged activations plus two ring stages must fit on chip
+  // (M = 9..16 at long K): the split count is raised if needed (a request, not
+  // a promise, as for the cluster GEMV).
+  constexpr int SG = Cfg::kStageGroups;
+  constexpr int kMinStages = SG > 2 ? SG : 2;
+  auto slice_rows = [&](int c) { return (((krows + c - 1) / c) + 7) / 8 * 8; };
+  while (C < kMaxRingCluster && layout(kMinStages, slice_rows(C)).total > smem_cap)
     C = std::min(kMaxRingCluster, C * 2);
   C = std::max(1, std::min(C, std::min(kMaxRingCluster, krows / 8)));
   int rows_per_cta = (((krows + C - 1) / C) + 7) / 8 * 8;
@@ -901,6 +921,16 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   int stages = std::min(nst, 12);
   while (stages > 1 && layout(stages, rows_per_cta).total > budget) --stages;
   if (stages < 1) stages = 1;
+  // Ring slots are reused (nst > stages) only with a stage count that is a
+  // multiple of the warp groups taking stages round-robin: then every slot
+  // belongs to one group, which waits on that slot's phases strictly in order.
+  // Otherwise a group could wait on a slot two phases ahead of its current one
+  // and the parity test of the mbarrier wait would pass early.
+  if (nst > stages) {
+    stages = stages / SG * SG;
+    if (stages < SG) stages = SG;
+  }
+  if (nst > stages && stages % SG != 0) return NG_ERR_BAD_SHAPE;
   if (layout(stages, rows_per_cta).total > smem_cap) return NG_ERR_BAD_SHAPE;
 
   CUtensorMap tmap;
