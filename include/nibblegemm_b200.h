@@ -109,9 +109,14 @@ int ng_dequant_w4(const int32_t* qweight, const uint16_t* scales, void* out, int
  *     (bf16 x) arithmetic, algo 5 on the tensor pipe (magic-number operands to
  *     mma.sync, fp32 accumulation, offsets removed by a correction MMA);
  *     `splits` 1..8 = K slices reduced in a cluster as above; 0 = algo 5 on
- *     M <= 4 with K % 128 == 0 and a workspace: stream-K (one CTA per SM,
- *     equal shares of 16-row blocks, split tiles finished through the
- *     workspace in CTA order); otherwise a heuristic K split.
+ *     M <= 4 with K % 128 == 0 and a workspace: one CTA per SM with equal
+ *     shares of 16-row blocks, split tiles finished through the workspace in
+ *     fixed order -- "head/tail" when the column tiles fill half the SMs or
+ *     more (tile CTAs stream each tile's first blocks, helper CTAs the rest),
+ *     stream-K over the tile-major block list otherwise (measured slower than
+ *     the clustered grid in a chain of launches where that grid leaves SMs
+ *     free, so the default uses these only for M = 3..4 on long K); a
+ *     heuristic K split when those do not apply.
  *   All are launched with programmatic stream serialisation: they start
  *   streaming their read-only weights while the previous kernel on the stream
  *   finishes, and read x / write y / touch the workspace only after it has.

@@ -420,8 +420,8 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
     }
   }
   // Default schedule (measured on B200, M <= 8, no cluster-kernel options):
-  //   * >= 96 column tiles (N >= 12288), M <= 8 and M >= 2 or K <= 4096: the ring with
-  //     one CTA per tile (its CTAs sweep the rows in lockstep);
+  //   * >= 96 column tiles (N >= 12288), M <= 8 and M >= 2 or K <= 4096: the ring
+  //     with one CTA per tile (its CTAs sweep the rows in lockstep);
   //   * M = 3..4 and a packed weight >= 12 MiB: the stream-K ring (all SMs);
   //   * M > 4 (up to 16): the ring with its own K split;
   //   * otherwise the cluster kernel.
@@ -429,6 +429,9 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
     const int tiles = (N + 127) / 128;
     const double wbytes = static_cast<double>(K) * N / 2.0;
     if (tiles >= 96 && M <= 8 && (M > 1 || K <= 4096)) {
+      // One K slice per tile: the grid leaves SMs free, where the next kernel's
+      // CTAs start streaming early (measured: faster in a chain than the
+      // all-SM head/tail plan, 9.3 vs 16.2 us at config 1).
       algo = 5;
       if (splits == 0) splits = 1;
     } else if (M > 4 || (M >= 3 && wbytes >= 12.0 * (1 << 20))) {  // includes M = 9..16

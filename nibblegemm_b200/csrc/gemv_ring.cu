@@ -596,6 +596,65 @@ struct SkPart {  // U blocks over P CTAs: the first r get q + 1, the rest q
   }
 };
 
+// Work plan, shared by host and device.  Two modes:
+//   * stream-K (ht = 0): the tile-major list of T x RT blocks split into equal
+//     contiguous ranges over the P CTAs (`part`); slot b = CTA b's published
+//     partial; the first CTA of a split tile finishes it.
+//   * head/tail (ht = 1, T < P): CTA t < T streams the first B0 blocks of tile
+//     t (its head, in lockstep with the other tile CTAs) and finishes the
+//     tile; the P - T helper CTAs split the tile-major list of tails (RT - B0
+//     blocks each) into equal contiguous ranges (`part`, at least a whole tail
+//     each, so a tail has at most two helpers) and publish to slot 2t + part,
+//     part 0 for the helper holding the tail's first block.  Balances the work
+//     per SM over all SMs while every CTA still sweeps rows in order.
+struct SkPlan {
+  int ht, T, RT, B0, P;
+  SkPart part;
+  // number of segments (runs of blocks inside one tile) of CTA b
+  __host__ __device__ int nseg(int b) const {
+    if (ht) {
+      if (b < T) return 1;
+      const int TL = RT - B0, v0 = part.start(b - T), v1 = part.start(b - T + 1);
+      return v1 > v0 ? (v1 - 1) / TL - v0 / TL + 1 : 0;
+    }
+    const int u0 = part.start(b), u1 = part.start(b + 1);
+    return u1 > u0 ? (u1 - 1) / RT - u0 / RT + 1 : 0;
+  }
+  // segment k of CTA b: tile, first block, blocks, role (0 store, 1 finish
+  // from slots [s_lo, s_hi], 2 publish to slot s_lo)
+  __host__ __device__ void seg(int b, int k, int& tile, int& blk0, int& nblk, int& role, int& s_lo,
+                      int& s_hi) const {
+    if (ht) {
+      const int TL = RT - B0;
+      if (b < T) {
+        tile = b, blk0 = 0, nblk = B0;
+        role = TL == 0 ? 0 : 1;
+        s_lo = 2 * tile;
+        s_hi = 2 * tile + (part.owner(tile * TL) != part.owner(tile * TL + TL - 1) ? 1 : 0);
+        return;
+      }
+      const int v0 = part.start(b - T), v1 = part.start(b - T + 1);
+      tile = v0 / TL + k;
+      const int lo = (v0 > tile * TL ? v0 : tile * TL), hi = (v1 < (tile + 1) * TL ? v1 : (tile + 1) * TL);
+      blk0 = B0 + lo - tile * TL, nblk = hi - lo, role = 2;
+      s_lo = s_hi = 2 * tile + (lo == tile * TL ? 0 : 1);
+      return;
+    }
+    const int u0 = part.start(b), u1 = part.start(b + 1);
+    tile = u0 / RT + k;
+    const int lo = (u0 > tile * RT ? u0 : tile * RT), hi = (u1 < (tile + 1) * RT ? u1 : (tile + 1) * RT);
+    blk0 = lo - tile * RT, nblk = hi - lo;
+    const bool starts = lo == tile * RT, ends = hi == (tile + 1) * RT;
+    role = starts && ends ? 0 : (starts ? 1 : 2);
+    if (role == 2) {
+      s_lo = s_hi = b;
+    } else {
+      s_lo = b + 1;
+      s_hi = part.owner((tile + 1) * RT - 1);
+    }
+  }
+};
+
 struct SkLayout {
   size_t ring, xs, sc, red, fin, total;
   __host__ __device__ SkLayout(int stages, int MT, int K, int groups) {
@@ -627,7 +686,7 @@ template <int MT, bool XBF16>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemv_ring_sk_kernel(const __grid_constant__ CUtensorMap tmap_q, const void* __restrict__ x,
                         const __half* __restrict__ scales, void* __restrict__ y, int M, int K,
-                        int N, int G, SkPart part, int stages, int sc_groups,
+                        int N, int G, SkPlan plan, int stages, int sc_groups,
                         float* __restrict__ ws_part, unsigned int* __restrict__ ws_flag,
                         unsigned int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -637,12 +696,9 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int krows = K >> 3;
-  const int RT = krows / kSkRB;  // blocks per tile
   const int b = blockIdx.x;
-  const int u0 = part.start(b), u1 = part.start(b + 1);
+  const int nseg = plan.nseg(b);
   const int GR = G / 8;  // packed rows per quantisation group
-  const int lg0 = (u0 * kSkRB) / GR;  // first linear (tile-major) group of the range
-  const int nlg = u1 > u0 ? (u1 * kSkRB - 1) / GR - lg0 + 1 : 0;
   const SkLayout L(stages, MT, K, sc_groups);
   unsigned char* ring = smem + L.ring;
   __half* xs = reinterpret_cast<__half*>(smem + L.xs);
@@ -662,27 +718,33 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == kSkCW) {
-    // ---------------- producer ----------------
+    // ---------------- producer: the segments' blocks, 8 per stage ----------------
     const uint64_t pol = make_evict_first_policy();
     int s = 0, issued = 0;
-    for (int u = u0; u < u1; ++s) {
-      const int tile = u / RT, rb = u - tile * RT;
-      const int n = min(kSkCW, min(RT - rb, u1 - u));
-      const int slot = s % stages;
-      if (s >= stages) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((s / stages) - 1) & 1, err, abort_flag);
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+    bool stop = false;
+    for (int k = 0; k < nseg && !stop; ++k) {
+      int tile, blk0, nblk, role, s_lo, s_hi;
+      plan.seg(b, k, tile, blk0, nblk, role, s_lo, s_hi);
+      for (int o = 0; o < nblk; o += kSkCW, ++s) {
+        const int n = min(kSkCW, nblk - o);
+        const int slot = s % stages;
+        if (s >= stages) {
+          bool ok = true;
+          if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((s / stages) - 1) & 1, err, abort_flag);
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+            stop = true;
+            break;
+          }
+        }
+        const int boxes = n * (kSkRB / kBoxRows);
+        if (lane == 0) mbar_arrive_expect_tx(&full[slot], boxes * (kBoxRows * kRCols * 4));
+        __syncwarp();
+        unsigned char* dst = ring + static_cast<size_t>(slot) * kSkStageBytes;
+        if (lane < boxes)
+          tma_box_g2s(dst + lane * (kBoxRows * kRCols * 4), &tmap_q, &full[slot], tile * kRCols,
+                      (blk0 + o) * kSkRB + lane * kBoxRows, pol);
+        issued = s + 1;
       }
-      const int boxes = n * (kSkRB / kBoxRows);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], boxes * (kBoxRows * kRCols * 4));
-      __syncwarp();
-      unsigned char* dst = ring + static_cast<size_t>(slot) * kSkStageBytes;
-      if (lane < boxes)
-        tma_box_g2s(dst + lane * (kBoxRows * kRCols * 4), &tmap_q, &full[slot], tile * kRCols,
-                    rb * kSkRB + lane * kBoxRows, pol);
-      issued = s + 1;
-      u += n;
     }
     if (lane == 0)
       for (int t = max(0, issued - stages); t < issued; ++t)
@@ -691,12 +753,21 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   }
 
   // ---------------- consumers ----------------
-  for (int i = tid; i < nlg * 32; i += kSkCW * 32) {
-    const int g = i >> 5, l = i & 31;
-    const int LG = lg0 + g;
-    const int tile = LG / (K / G), gi = LG - tile * (K / G);
-    const int col = tile * kRCols + l * 4;
-    if (col < N) cp_async_8(ssm + g * kRCols + l * 4, scales + static_cast<size_t>(gi) * N + col);
+  // Scales of every segment, packed segment after segment.
+  {
+    int base = 0;
+    for (int k = 0; k < nseg; ++k) {
+      int tile, blk0, nblk, role, s_lo, s_hi;
+      plan.seg(b, k, tile, blk0, nblk, role, s_lo, s_hi);
+      const int gs = (blk0 * kSkRB) / GR, ge = ((blk0 + nblk) * kSkRB - 1) / GR;
+      for (int i = tid; i < (ge - gs + 1) * 32; i += kSkCW * 32) {
+        const int gg = i >> 5, l = i & 31;
+        const int col = tile * kRCols + l * 4;
+        if (col < N)
+          cp_async_8(ssm + (base + gg) * kRCols + l * 4, scales + static_cast<size_t>(gs + gg) * N + col);
+      }
+      base += ge - gs + 1;
+    }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -731,138 +802,135 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   for (int r = 0; r < 4; ++r) cv[r] = 0.f;
 
   constexpr int E = MT * kRCols;
-  int s = 0;
+  constexpr size_t kSlot = kSkMaxM * kRCols;  // floats per workspace slot
+  unsigned short* yo = static_cast<unsigned short*>(y);
+  int s = 0, base = 0;
   bool aborted = false;
-  for (int u = u0; u < u1; ++s) {
-    const int tile = u / RT, rb = u - tile * RT;
-    const int n = min(kSkCW, min(RT - rb, u1 - u));
-    const int slot = s % stages;
-    if (!aborted && !mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) aborted = true;
-    if (!aborted && warp < n) {
-      const int row0 = (rb + warp) * kSkRB;  // tile row of this warp's block
-      const unsigned char* blk = ring + static_cast<size_t>(slot) * kSkStageBytes +
-                                 warp * (kSkRB * kRCols * 4);
+  for (int k = 0; k < nseg; ++k) {
+    int tile, blk0, nblk, role, s_lo, s_hi;
+    plan.seg(b, k, tile, blk0, nblk, role, s_lo, s_hi);
+    const int gs = (blk0 * kSkRB) / GR;
+    for (int o = 0; o < nblk; o += kSkCW, ++s) {
+      const int n = min(kSkCW, nblk - o);
+      const int slot = s % stages;
+      if (!aborted && !mbar_wait_bounded(&full[slot], (s / stages) & 1, err, abort_flag)) aborted = true;
+      if (!aborted && warp < n) {
+        const int row0 = (blk0 + o + warp) * kSkRB;  // tile row of this warp's block
+        const unsigned char* blk = ring + static_cast<size_t>(slot) * kSkStageBytes +
+                                   warp * (kSkRB * kRCols * 4);
 #pragma unroll
-      for (int step = 0; step < kSkRB / 4; ++step) {
-        const int row = row0 + 4 * step;
-        const unsigned char* src = blk + (4 * step + t) * (kRCols * 4);
-        uint4 w[4];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          w[2 * h] = *reinterpret_cast<const uint4*>(src + (64 * h + 4 * g) * 4);
-          w[2 * h + 1] = *reinterpret_cast<const uint4*>(src + (64 * h + 32 + 4 * g) * 4);
-        }
-        uint4 xv = make_uint4(0u, 0u, 0u, 0u);
-        if (g < MT) xv = *reinterpret_cast<const uint4*>(xs + static_cast<size_t>(g) * K + (row + t) * 8);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t wa[4] = {w[2 * h].x, w[2 * h].y, w[2 * h].z, w[2 * h].w};
-          const uint32_t wb[4] = {w[2 * h + 1].x, w[2 * h + 1].y, w[2 * h + 1].z, w[2 * h + 1].w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t ha[4], hb[4];
-            decode_mma_operands<XBF16>(wa[i], ha);
-            decode_mma_operands<XBF16>(wb[i], hb);
-            ring_mma<XBF16>(c[h][i], ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
-            ring_mma<XBF16>(c[h][i], ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
-          }
-        }
-        ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.x, xv.y);
-        ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.z, xv.w);
-        if ((row + 4) % GR == 0 || step == kSkRB / 4 - 1) {  // group or block end
-          const int lg = ((tile * krows + row) * 8) / G - lg0;
-          const __half* sg = ssm + lg * kRCols;
+        for (int step = 0; step < kSkRB / 4; ++step) {
+          const int row = row0 + 4 * step;
+          const unsigned char* src = blk + (4 * step + t) * (kRCols * 4);
+          uint4 w[4];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const uint2 sa = *reinterpret_cast<const uint2*>(sg + 64 * h + 4 * g);
-            const uint2 sb = *reinterpret_cast<const uint2*>(sg + 64 * h + 32 + 4 * g);
-            const float2 a01 = __half22float2(h2_from_bits(sa.x)), a23 = __half22float2(h2_from_bits(sa.y));
-            const float2 b01 = __half22float2(h2_from_bits(sb.x)), b23 = __half22float2(h2_from_bits(sb.y));
-            const float fa[4] = {a01.x, a01.y, a23.x, a23.y};
-            const float fb[4] = {b01.x, b01.y, b23.x, b23.y};
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-              for (int r = 0; r < 4; ++r) {
-                if (MT == 1 && (r & 1)) continue;
-                tot[h][i][r] = fmaf(r < 2 ? fa[i] : fb[i], c[h][i][r] - cv[r & 1], tot[h][i][r]);
-                c[h][i][r] = 0.f;
-              }
+            w[2 * h] = *reinterpret_cast<const uint4*>(src + (64 * h + 4 * g) * 4);
+            w[2 * h + 1] = *reinterpret_cast<const uint4*>(src + (64 * h + 32 + 4 * g) * 4);
           }
+          uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+          if (g < MT) xv = *reinterpret_cast<const uint4*>(xs + static_cast<size_t>(g) * K + (row + t) * 8);
 #pragma unroll
-          for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t wa[4] = {w[2 * h].x, w[2 * h].y, w[2 * h].z, w[2 * h].w};
+            const uint32_t wb[4] = {w[2 * h + 1].x, w[2 * h + 1].y, w[2 * h + 1].z, w[2 * h + 1].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t ha[4], hb[4];
+              decode_mma_operands<XBF16>(wa[i], ha);
+              decode_mma_operands<XBF16>(wb[i], hb);
+              ring_mma<XBF16>(c[h][i], ha[0], hb[0], ha[1], hb[1], xv.x, xv.y);
+              ring_mma<XBF16>(c[h][i], ha[2], hb[2], ha[3], hb[3], xv.z, xv.w);
+            }
+          }
+          ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.x, xv.y);
+          ring_mma<XBF16>(cv, kC0, kC0, kC1, kC1, xv.z, xv.w);
+          if ((row + 4) % GR == 0 || step == kSkRB / 4 - 1) {  // group or block end
+            const __half* sg = ssm + (base + row / GR - gs) * kRCols;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint2 sa = *reinterpret_cast<const uint2*>(sg + 64 * h + 4 * g);
+              const uint2 sb = *reinterpret_cast<const uint2*>(sg + 64 * h + 32 + 4 * g);
+              const float2 a01 = __half22float2(h2_from_bits(sa.x)), a23 = __half22float2(h2_from_bits(sa.y));
+              const float2 b01 = __half22float2(h2_from_bits(sb.x)), b23 = __half22float2(h2_from_bits(sb.y));
+              const float fa[4] = {a01.x, a01.y, a23.x, a23.y};
+              const float fb[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                  if (MT == 1 && (r & 1)) continue;
+                  tot[h][i][r] = fmaf(r < 2 ? fa[i] : fb[i], c[h][i][r] - cv[r & 1], tot[h][i][r]);
+                  c[h][i][r] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) cv[r] = 0.f;
+          }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    base += ((blk0 + nblk) * kSkRB - 1) / GR - gs + 1;
 
-    if (rb + n == RT || u + n == u1) {
-      // ---- segment end: this CTA's share of `tile` is complete ----
-      const int t0 = tile * RT;
-      const bool starts_at_0 = u0 <= t0;
-      const bool whole = starts_at_0 && u1 >= t0 + RT;
+    // ---- segment end: this CTA's share of `tile` is complete ----
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int m = 2 * t + (r & 1);
-            const int col = 64 * h + (r < 2 ? 0 : 32) + 4 * g + i;
-            if (m < MT) red[(warp * MT + m) * kRCols + col] = tot[h][i][r];
-            tot[h][i][r] = 0.f;
-          }
-      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (1) warp partials visible
-      unsigned short* yo = static_cast<unsigned short*>(y);
-      auto store = [&](int e, float v) {
-        const int m = e / kRCols, cn = tile * kRCols + (e % kRCols);
-        if (m < M && cn < N)
-          yo[static_cast<size_t>(m) * N + cn] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
-                                                      : __half_as_ushort(__float2half_rn(v));
-      };
-      for (int e = tid; e < E; e += kSkCW * 32) {
-        float v = 0.f;
+        for (int r = 0; r < 4; ++r) {
+          const int m = 2 * t + (r & 1);
+          const int col = 64 * h + (r < 2 ? 0 : 32) + 4 * g + i;
+          if (m < MT) red[(warp * MT + m) * kRCols + col] = tot[h][i][r];
+          tot[h][i][r] = 0.f;
+        }
+    asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (1) warp partials visible
+    auto store = [&](int e, float v) {
+      const int m = e / kRCols, cn = tile * kRCols + (e % kRCols);
+      if (m < M && cn < N)
+        yo[static_cast<size_t>(m) * N + cn] = XBF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                                    : __half_as_ushort(__float2half_rn(v));
+    };
+    for (int e = tid; e < E; e += kSkCW * 32) {
+      float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kSkCW; ++w) v += red[w * E + e];
-        if (whole)
-          store(e, v);
-        else if (starts_at_0)
-          fin[e] = v;
-        else
-          ws_part[static_cast<size_t>(b) * (kSkMaxM * kRCols) + e] = v;
-      }
-      if (!whole && !starts_at_0) __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (2)
-      if (!whole && !starts_at_0) {
-        if (tid == 0) sk_st_release(&ws_flag[b], 1u);
-      } else if (!whole) {
-        // finisher: the later CTAs holding the rest of the tile
-        const int last = part.owner(t0 + RT - 1);
-        if (tid == 0) {
-          for (int o = b + 1; o <= last; ++o) {
-            const uint64_t ts = global_timer_ns();
-            while (sk_ld_acquire(&ws_flag[o]) == 0u) {
-              if (global_timer_ns() - ts > 1000000000ull) {
-                atomicOr(err, kErrWaitTimeout);
-                break;
-              }
+      for (int w = 0; w < kSkCW; ++w) v += red[w * E + e];
+      if (role == 0)
+        store(e, v);
+      else if (role == 1)
+        fin[e] = v;
+      else
+        ws_part[static_cast<size_t>(s_lo) * kSlot + e] = v;
+    }
+    if (role == 2) __threadfence();
+    asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (2)
+    if (role == 2) {
+      if (tid == 0) sk_st_release(&ws_flag[s_lo], 1u);
+    } else if (role == 1) {
+      if (tid == 0) {
+        for (int o = s_lo; o <= s_hi; ++o) {
+          const uint64_t ts = global_timer_ns();
+          while (sk_ld_acquire(&ws_flag[o]) == 0u) {
+            if (global_timer_ns() - ts > 1000000000ull) {
+              atomicOr(err, kErrWaitTimeout);
+              break;
             }
           }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
-        for (int e = tid; e < E; e += kSkCW * 32) {
-          float v = fin[e];
-          for (int o = b + 1; o <= last; ++o) v += __ldcg(ws_part + static_cast<size_t>(o) * (kSkMaxM * kRCols) + e);
-          store(e, v);
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
-        if (tid == 0)
-          for (int o = b + 1; o <= last; ++o) ws_flag[o] = 0u;
       }
-      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (3) red / fin reusable
+      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
+      for (int e = tid; e < E; e += kSkCW * 32) {
+        float v = fin[e];
+        for (int o = s_lo; o <= s_hi; ++o) v += __ldcg(ws_part + static_cast<size_t>(o) * kSlot + e);
+        store(e, v);
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");
+      if (tid == 0)
+        for (int o = s_lo; o <= s_hi; ++o) ws_flag[o] = 0u;
     }
-    u += n;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSkCW * 32) : "memory");  // (3) red / fin reusable
   }
 }
 
@@ -993,11 +1061,31 @@ int ring_mma_dispatch(const void* x, const uint32_t* qw, const __half* s, void* 
 size_t sk_ws_offset(int N, const DeviceInfo& dev) {
   return (gemv_tc_workspace_bytes(N, dev) + 255) / 256 * 256;
 }
-size_t sk_ws_bytes(const DeviceInfo& dev) {
-  return static_cast<size_t>(dev.sm_count) * (kSkMaxM * kRCols * 4 + 4);
+size_t sk_ws_bytes(const DeviceInfo& dev) {  // 2 x SMs slots (head/tail uses 2 per tile) + flags
+  return static_cast<size_t>(2 * dev.sm_count) * (kSkMaxM * kRCols * 4 + 4);
 }
 
-// Returns NG_OK, an error, or -1 when the stream-K variant does not apply.
+// The work plan for an N x K weight: head/tail when the tiles fill between
+// half and all of the SMs and every helper's share covers a whole tail,
+// stream-K otherwise.  Returns false when neither applies.
+bool make_sk_plan(int tiles, int RT, int sms, SkPlan* plan) {
+  const int U = tiles * RT;
+  if (tiles * 2 >= sms && tiles < sms && RT >= 2) {
+    const int H = sms - tiles;
+    int B0 = (tiles * RT + sms / 2) / sms;  // blocks per SM if all SMs did the same
+    B0 = B0 < 1 ? 1 : (B0 > RT - 1 ? RT - 1 : B0);
+    const int TL = RT - B0, tail = tiles * TL;
+    if (tail / H >= TL) {
+      *plan = SkPlan{1, tiles, RT, B0, sms, SkPart{tail / H, tail % H}};
+      return true;
+    }
+  }
+  const int P = sms < U ? sms : U;
+  *plan = SkPlan{0, tiles, RT, 0, P, SkPart{U / P, U % P}};
+  return true;
+}
+
+// Returns NG_OK, an error, or -1 when the stream-K ring does not apply.
 template <int MT, bool XBF16>
 int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N,
                 int G, void* ws, size_t ws_bytes, const DeviceInfo& dev, cudaStream_t stream) {
@@ -1008,13 +1096,24 @@ int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int
   if (ws == nullptr || ws_bytes < off + sk_ws_bytes(dev)) return -1;
   const int RT = krows / kSkRB;
   const int tiles = (N + kRCols - 1) / kRCols;
-  const int U = tiles * RT;
-  const int P = std::min(dev.sm_count, U);
-  SkPart part{U / P, U % P};
-  const int sc_groups = ((part.q + 1) * kSkRB) / (G / 8) + 2;
+  SkPlan plan;
+  if (!make_sk_plan(tiles, RT, dev.sm_count, &plan)) return -1;
+  const int P = plan.P;
+  // shared-memory scale rows and ring depth: the largest any CTA needs
+  int sc_groups = 1, max_blocks = 1;
+  for (int b = 0; b < P; ++b) {
+    int groups = 0, blocks = 0;
+    for (int k = 0; k < plan.nseg(b); ++k) {
+      int tile, blk0, nblk, role, s_lo, s_hi;
+      plan.seg(b, k, tile, blk0, nblk, role, s_lo, s_hi);
+      groups += ((blk0 + nblk) * kSkRB - 1) / (G / 8) - (blk0 * kSkRB) / (G / 8) + 1;
+      blocks += (nblk + kSkCW - 1) / kSkCW;  // stages of this segment
+    }
+    sc_groups = std::max(sc_groups, groups);
+    max_blocks = std::max(max_blocks, blocks);
+  }
   const size_t smem_cap = dev.smem_optin ? dev.smem_optin : 227 * 1024;
-  const int want = (part.q + 1 + kSkCW - 1) / kSkCW + 1;  // stages a range can span
-  int stages = std::min(4, want);
+  int stages = std::min(4, max_blocks);
   while (stages > 1 && SkLayout(stages, MT, K, sc_groups).total > smem_cap) --stages;
   const size_t smem = SkLayout(stages, MT, K, sc_groups).total;
   if (smem > smem_cap) return -1;
@@ -1038,7 +1137,8 @@ int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int
       return NG_ERR_CUDA;
   }
   float* ws_part = reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + off);
-  unsigned int* ws_flag = reinterpret_cast<unsigned int*>(ws_part + static_cast<size_t>(dev.sm_count) * kSkMaxM * kRCols);
+  unsigned int* ws_flag =
+      reinterpret_cast<unsigned int*>(ws_part + static_cast<size_t>(2 * dev.sm_count) * kSkMaxM * kRCols);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(P, 1, 1);
   cfg.blockDim = dim3(kSkThreads, 1, 1);
@@ -1051,7 +1151,7 @@ int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return launch_status(cudaLaunchKernelEx(&cfg, kern, tmap, x, s, y, M, K, N, G, part, stages,
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, tmap, x, s, y, M, K, N, G, plan, stages,
                                           sc_groups, ws_part, ws_flag, dev.err));
 }
 
