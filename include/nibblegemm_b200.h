@@ -164,7 +164,8 @@ int ng_gemv_w4a16_noalloc(const void* x, int x_dtype, const int32_t* qweight,
  * (csrc/gemm_w4a16.cu:379-429, bound at csrc/bindings.cpp:16-18).
  *   Any M >= 1; K % 64 == 0; N % 4 == 0; group_size in {64, 128, 256};
  *   x, qweight 16-byte aligned; scales 2-byte aligned.
- *   tile_tokens: 0 = heuristic, else 16, 32, 64, 128 or 256 rows of X per tile.
+ *   tile_tokens: 0 = heuristic, else 16, 32, 64, 128, 192, 224, 240 or 256 rows
+ *   of X per tile.
  *   workspace (may be NULL): ng_gemm_workspace_bytes(M, N) bytes, 256-byte
  *   aligned, zero-filled before first use.  With it, grids that would leave
  *   SMs idle (few tiles: small M, or N = 4096 with long K) are split along K;

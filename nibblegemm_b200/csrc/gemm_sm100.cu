@@ -63,6 +63,15 @@ struct Barriers {
   int last;  // split-K: this CTA's epilogue finishes the current tile
 };
 
+// tcgen05.alloc takes a power-of-two column count in [32, 512]: the two
+// BT-column accumulators are placed in the smallest such allocation.
+template <int BT>
+constexpr uint32_t tmem_cols() {
+  uint32_t c = 32;
+  while (c < 2u * BT) c <<= 1;
+  return c;
+}
+
 template <int BT, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
@@ -104,7 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_x);
     tma_prefetch_desc(&tmap_q);
   }
-  if (warp == 2) tmem_alloc(&bars->tmem_slot, 2 * BT);
+  static_assert(tmem_cols<BT>() <= 512, "two accumulators must fit in tensor memory");
+  if (warp == 2) tmem_alloc(&bars->tmem_slot, tmem_cols<BT>());
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -317,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BT);
+    tmem_dealloc(tmem_base, tmem_cols<BT>());
   }
 }
 
@@ -405,6 +415,9 @@ int dispatch_bt(int bt, const void* x, const int32_t* q, const __half* s, void* 
     case 32: return run_gemm<32, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
     case 64: return run_gemm<64, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
     case 128: return run_gemm<128, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    case 192: return run_gemm<192, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    case 224: return run_gemm<224, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
+    case 240: return run_gemm<240, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
     default: return run_gemm<256, BF16>(x, q, s, y, M, K, N, G, ws, wsb, dev, st);
   }
 }
@@ -422,6 +435,10 @@ int pick_bt(int M, int N, int sm_count) {
     const long long waves = (tiles + sm_count - 1) / sm_count;
     return waves * (bt + 32);  // per-tile time ~ BT plus a fixed pipeline fill
   };
+  // 192 / 224 / 240 (multiples of 16 and of the 8-row swizzle atom) are
+  // accepted as tile_tokens but not picked: they fill the last wave better, yet
+  // measured no faster at M = 2048 and slower at M = 8192 -- the k-step time is
+  // set by shared-memory traffic and decode, which do not shrink with BT.
   return cost(128) < cost(256) ? 128 : 256;
 }
 
@@ -449,7 +466,8 @@ extern "C" int ng_gemm_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
   if (static_cast<long long>(M) * N >= (1LL << 40) || K / 8 > (1 << 30)) return NG_ERR_BAD_SHAPE;
   if (tile_tokens != 0 && tile_tokens != 16 && tile_tokens != 32 && tile_tokens != 64 &&
-      tile_tokens != 128 && tile_tokens != 256)
+      tile_tokens != 128 && tile_tokens != 192 && tile_tokens != 224 && tile_tokens != 240 &&
+      tile_tokens != 256)
     return NG_ERR_BAD_ARGUMENT;
   if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 2) || !aligned(y, 2) ||
       !aligned(workspace, 256))

@@ -66,7 +66,7 @@ def test_gemm_edges_match_oracle(M, N, G):
     check(y, oracle(x, q, s, G, K, "f16"), torch.float16)
 
 
-@pytest.mark.parametrize("bt", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("bt", [16, 32, 64, 128, 192, 224, 240, 256])
 @pytest.mark.parametrize("act", ["f16", "bf16"])
 def test_every_token_tile(bt, act):
     M, K, N, G = 300, 1024, 392, 128
