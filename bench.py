@@ -49,6 +49,7 @@ WORKLOADS = {
     "gemv": dict(M=1, K=4096, N=14336, G=128, name="W4A16 decode GEMV M=1 K=4096 N=14336 g128 fp16 (BASELINE config 1)"),
     "gemm": dict(M=2048, K=4096, N=14336, G=128, name="W4A16 prefill GEMM M=2048 K=4096 N=14336 g128 fp16 (BASELINE config 3)"),
     "step8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 projection stack (224 projections), batch 1, tensor-parallel over the ranks"),
+    "decode8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 full decode step (BASELINE config 4): attention over a 1024-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch 1, tensor-parallel over the ranks"),
     "sweep2": dict(M=1, K=4096, N=14336, G=128, name="BASELINE config 2: decode GEMV sweep M x (K, N), eager and graph, vs cuBLAS fp16"),
     "sweep3": dict(M=2048, K=4096, N=14336, G=128, name="BASELINE config 3: prefill GEMM sweep M x (K, N) x {fp16, bf16}"),
 }
@@ -285,6 +286,104 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_decode(args, wl, world, rank, local, dist):
+    """Tokens/s of the full Llama-3-8B decode step.
+
+    One step = one token through embedding, 32 layers (RMSNorm, fused q|k|v
+    GEMV, RoPE + KV append, GQA attention over 1024 cached positions, o GEMV,
+    all-reduce, RMSNorm, fused gate|up GEMV, SwiGLU, down GEMV, all-reduce),
+    final norm, fp16 lm_head and argmax; captured once in a CUDA graph and
+    replayed with the position held at 1023 (context 1024).  Strong scaling.
+    """
+    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, Llama3Decoder
+    cfg = LLAMA3_8B_MODEL
+    m = Llama3Decoder(cfg, batch=1, max_ctx=1024, rank=rank, world=world, reduce=args.reduce)
+    m.pos.fill_(1023)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            m.step(advance=False)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        m.step(advance=False)
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for _ in range(100):  # fixed count on every rank: the graph holds collectives
+            graph.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    per_ms = ms / args.steps
+    # e2e: the token id in from pinned host memory, the step (graph), the next id back
+    tok_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+    out_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            m.tokens.copy_(tok_host, non_blocking=True)
+            graph.replay()
+            out_host.copy_(m.tokens, non_blocking=True)
+            stream.synchronize()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    if rank == 0:
+        hbm, _, src = measured_peaks()
+        kv = 2 * cfg["layers"] * 1024 * m.hkv * cfg["head_dim"] * 2
+        nbytes = m.weight_bytes + m.lm_head.numel() * 2 + kv + cfg["hidden"] * 2
+        achieved = nbytes / (per_ms * 1e-3) / 1e9
+        # ours per layer: 2 norms, 4 GEMVs, RoPE, 2 attention, SwiGLU (+2 peer all-reduces); final norm
+        launches = 32 * 10 + 1 + (64 if (world > 1 and args.reduce == "peer") else 0)
+        line = {
+            "metric": METRIC, "value": round(1000.0 / per_ms, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic random-init Llama-3-8B (seeded N(0,0.02) weights, RTN INT4 g128), batch 1",
+            "config": {"workload": wl["name"], "layers": 32, "hidden": 4096, "heads": 32, "kv_heads": 8,
+                       "intermediate": 14336, "vocab": 128256, "context": 1024, "group_size": 128,
+                       "batch": 1, "parallelism": f"tp{world}",
+                       "tp_reduce": (args.reduce if world > 1 else None),
+                       "l2": "4.8 GB read per token (>> L2)",
+                       "timing": "one CUDA graph per token, replayed `steps` times"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": None,
+                         "peak_source": f"{src} copy bandwidth", "algorithmic_bytes_per_step_per_rank": nbytes},
+            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 8, "path": "token id in -> Llama3Decoder.step() graph -> next id out"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
 def run_step(args, wl, world, rank, local, dist):
     """Tokens/s of the Llama-3-8B INT4 projection stack.
 
@@ -412,6 +511,8 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.workload == "step8b":
         return run_step(args, wl, world, rank, local, dist)
+    if args.workload == "decode8b":
+        return run_decode(args, wl, world, rank, local, dist)
     if args.workload in ("sweep2", "sweep3"):
         if rank == 0:
             run_sweep(args, local)

@@ -208,6 +208,35 @@ int ng_ipc_free(void* dev_ptr);
 int ng_ipc_open(const void* handle, void** dev_ptr);
 int ng_ipc_close(void* dev_ptr);
 
+/*
+ * Decode-step kernels around the projections (no counterpart in the reference,
+ * whose decode step is projections only; bench/bench_model.py:57-86).  All
+ * take fp16 or bf16 activations (`dtype`), compute in fp32, enqueue on
+ * `stream` and allocate nothing.
+ *   ng_rmsnorm: per token h = x + residual (residual may be NULL; else h is
+ *     written back to it), y = h * rsqrt(mean(h^2) + eps) * weight.  [M, H].
+ *   ng_rope_append: qkv [M, (Hq + 2 Hkv) * D] -> q_out [M, Hq, D] with RoPE
+ *     ("rotate half" pairs (i, i + D/2), angle pos * theta^(-2i/D)), K rows
+ *     rotated and V rows copied into k_cache / v_cache [max_ctx, Hkv, D] at
+ *     row pos[m] (device int array of M positions; rows outside [0, max_ctx)
+ *     are not written).
+ *   ng_attn_decode: GQA attention of q [M, Hq, D] (D = 128) over the first
+ *     min(ctx_len[m], max_ctx) cache rows (device int array), softmax scale; the
+ *     context is split in `splits` chunks whose fp32 partials
+ *     (ng_attn_workspace_bytes) are combined in chunk order -> out [M, Hq, D].
+ *   ng_silu_mul: gate_up [M, 2I] (gate | up) -> out [M, I] = silu(gate) * up.
+ */
+int ng_rmsnorm(const void* x, void* residual, const void* weight, void* y, int dtype, int M, int H,
+               float eps, void* stream);
+int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache, const int* pos,
+                   int dtype, int M, int Hq, int Hkv, int D, float theta, int max_ctx,
+                   void* stream);
+size_t ng_attn_workspace_bytes(int M, int Hq, int splits);
+int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int* ctx_len,
+                   void* out, int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,
+                   float scale, void* workspace, size_t workspace_bytes, void* stream);
+int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int I, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

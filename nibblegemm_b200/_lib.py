@@ -27,6 +27,12 @@ SIGNATURES = {
     "ng_gemv_w4a16": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P]),
     "ng_gemv_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
     "ng_gemv_w4a16_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "ng_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _P]),
+    "ng_rope_append": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P]),
+    "ng_attn_workspace_bytes": (ctypes.c_size_t, [_I, _I, _I]),
+    "ng_attn_decode": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P,
+                            ctypes.c_size_t, _P]),
+    "ng_silu_mul": (_I, [_P, _P, _I, _I, _I, _P]),
     "ng_allreduce_buffer_bytes": (ctypes.c_size_t, [_I, ctypes.c_size_t]),
     "ng_allreduce_sum": (_I, [_P, _I, ctypes.c_size_t, _P, _I, _I, ctypes.c_size_t, _P, _P]),
     "ng_ipc_alloc": (_I, [ctypes.c_size_t, _P, _P]),

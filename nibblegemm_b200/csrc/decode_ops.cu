@@ -1,0 +1,259 @@
+// Non-GEMM kernels of a Llama-style decode step (batch M <= 16 tokens, one
+// position each): fused residual + RMSNorm, RoPE + KV-cache append, GQA
+// decode attention (split over the context, then combined), SwiGLU.  All are
+// HBM- or latency-bound elementwise / reduction kernels; activations are
+// fp16 or bf16 with fp32 arithmetic.  Each entry point validates its
+// arguments, enqueues on the caller's stream and returns an NG_* status.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "ng_common.cuh"
+
+namespace ngb {
+namespace {
+
+template <bool BF16>
+__device__ __forceinline__ float ld_act(const void* p, size_t i) {
+  const unsigned short v = static_cast<const unsigned short*>(p)[i];
+  return BF16 ? __uint_as_float(static_cast<uint32_t>(v) << 16) : __half2float(__ushort_as_half(v));
+}
+template <bool BF16>
+__device__ __forceinline__ void st_act(void* p, size_t i, float v) {
+  static_cast<unsigned short*>(p)[i] =
+      BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];  // fixed order: deterministic
+  return t;
+}
+
+// h = x + residual (if residual != null; h is written back to residual),
+// y = h * rsqrt(mean(h^2) + eps) * w.  One CTA per token.
+template <bool BF16>
+__global__ void rmsnorm_kernel(const void* __restrict__ x, void* __restrict__ residual,
+                               const void* __restrict__ w, void* __restrict__ y, int H, float eps) {
+  __shared__ float red[32];
+  const size_t base = static_cast<size_t>(blockIdx.x) * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float h = ld_act<BF16>(x, base + i);
+    if (residual) h += ld_act<BF16>(residual, base + i);
+    ss += h * h;
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / static_cast<float>(H) + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float h = ld_act<BF16>(x, base + i);
+    if (residual) {
+      h += ld_act<BF16>(residual, base + i);
+      st_act<BF16>(residual, base + i, h);
+    }
+    st_act<BF16>(y, base + i, h * inv * ld_act<BF16>(w, i));
+  }
+}
+
+// qkv[M, (Hq + 2 Hkv) * D] -> q[M, Hq, D] with RoPE, and K / V rows of every
+// token appended at its position: cache[pos, Hkv, D].  Rotary pairs (i,
+// i + D/2) ("rotate half"), angle pos * theta^(-2i/D) computed in fp32.
+template <bool BF16>
+__global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restrict__ q_out,
+                                   void* __restrict__ k_cache, void* __restrict__ v_cache,
+                                   const int* __restrict__ pos, int Hq, int Hkv, int D, float theta,
+                                   int max_ctx) {
+  const int m = blockIdx.y, head = blockIdx.x;  // head in [0, Hq + Hkv): q heads then k heads
+  const int p = pos[m];
+  const bool in_cache = p >= 0 && p < max_ctx;  // cache rows outside [0, max_ctx) are never written
+  if (head >= Hq && !in_cache) return;
+  const int row = (Hq + 2 * Hkv) * D;
+  const size_t src = static_cast<size_t>(m) * row + static_cast<size_t>(head) * D;
+  const int half = D / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float inv_freq = exp2f(-2.f * i / D * log2f(theta));
+    float sn, cs;
+    sincosf(static_cast<float>(p) * inv_freq, &sn, &cs);
+    const float a = ld_act<BF16>(qkv, src + i), b = ld_act<BF16>(qkv, src + i + half);
+    const float ra = a * cs - b * sn, rb = b * cs + a * sn;
+    if (head < Hq) {
+      const size_t dst = (static_cast<size_t>(m) * Hq + head) * D;
+      st_act<BF16>(q_out, dst + i, ra);
+      st_act<BF16>(q_out, dst + i + half, rb);
+    } else {
+      const int kh = head - Hq;
+      const size_t dst = (static_cast<size_t>(p) * Hkv + kh) * D;
+      st_act<BF16>(k_cache, dst + i, ra);
+      st_act<BF16>(k_cache, dst + i + half, rb);
+    }
+  }
+  if (head >= Hq) {  // V rows: copied unrotated
+    const int kh = head - Hq;
+    const size_t vsrc = static_cast<size_t>(m) * row + static_cast<size_t>(Hq + Hkv + kh) * D;
+    const size_t dst = (static_cast<size_t>(p) * Hkv + kh) * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+      static_cast<unsigned short*>(v_cache)[dst + i] = static_cast<const unsigned short*>(qkv)[vsrc + i];
+  }
+}
+
+// Split-context GQA decode attention, D = 128.  Grid (Hkv, splits, M): a CTA
+// owns one KV head, one contiguous chunk of the context and one token; its
+// G = Hq / Hkv warps are the query heads sharing that KV head (lane l holds
+// dims 4l..4l+3).  Online softmax in fp32; partial (max, sum, acc[D]) per
+// (token, q head, split) go to the workspace for the combine kernel.
+constexpr int kAttnD = 128;
+template <bool BF16>
+__global__ void attn_partial_kernel(const void* __restrict__ q, const void* __restrict__ k_cache,
+                                    const void* __restrict__ v_cache, const int* __restrict__ ctx,
+                                    float* __restrict__ part, int Hq, int Hkv, int chunk,
+                                    int splits, float scale, int max_ctx) {
+  const int kh = blockIdx.x, sp = blockIdx.y, m = blockIdx.z;
+  const int G = Hq / Hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qh = kh * G + warp;
+  const int len = min(ctx[m], max_ctx);  // never read past the cache
+  const int t0 = sp * chunk, t1 = min(len, t0 + chunk);
+  float qv[4];
+  const size_t qb = (static_cast<size_t>(m) * Hq + qh) * kAttnD + lane * 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qv[j] = ld_act<BF16>(q, qb + j) * scale;
+  float mx = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int t = t0; t < t1; ++t) {
+    const size_t kb = (static_cast<size_t>(t) * Hkv + kh) * kAttnD + lane * 4;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += qv[j] * ld_act<BF16>(k_cache, kb + j);
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(mx, s);
+    const float corr = __expf(mx - nm), pw = __expf(s - nm);
+    sum = sum * corr + pw;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * ld_act<BF16>(v_cache, kb + j);
+    mx = nm;
+  }
+  // part layout: [M][Hq][splits][2 + D]
+  float* o = part + ((static_cast<size_t>(m) * Hq + qh) * splits + sp) * (2 + kAttnD);
+  if (lane == 0) {
+    o[0] = mx;
+    o[1] = sum;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[2 + lane * 4 + j] = acc[j];
+}
+
+// Combine the splits of one (token, q head) in split order: out[M, Hq, D].
+template <bool BF16>
+__global__ void attn_combine_kernel(const float* __restrict__ part, void* __restrict__ out,
+                                    int Hq, int splits) {
+  const int qh = blockIdx.x, m = blockIdx.y, d = threadIdx.x;  // blockDim = D
+  const float* p = part + (static_cast<size_t>(m) * Hq + qh) * splits * (2 + kAttnD);
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, p[s * (2 + kAttnD)]);
+  float den = 0.f, num = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float ms = p[s * (2 + kAttnD)];
+    if (ms == -INFINITY) continue;  // empty split
+    const float w = __expf(ms - mx);
+    den += w * p[s * (2 + kAttnD) + 1];
+    num += w * p[s * (2 + kAttnD) + 2 + d];
+  }
+  st_act<BF16>(out, (static_cast<size_t>(m) * Hq + qh) * kAttnD + d, num / den);
+}
+
+// gate_up[M, 2I] (gate | up) -> out[M, I] = silu(gate) * up.
+template <bool BF16>
+__global__ void silu_mul_kernel(const void* __restrict__ gu, void* __restrict__ out, int M, int I) {
+  const size_t n = static_cast<size_t>(M) * I;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t m = i / I, j = i - m * I;
+    const float g = ld_act<BF16>(gu, m * 2 * I + j), u = ld_act<BF16>(gu, m * 2 * I + I + j);
+    st_act<BF16>(out, i, g / (1.f + __expf(-g)) * u);
+  }
+}
+
+bool dtype_ok(int d) { return d == NG_DTYPE_F16 || d == NG_DTYPE_BF16; }
+
+}  // namespace
+}  // namespace ngb
+
+using namespace ngb;
+
+extern "C" int ng_rmsnorm(const void* x, void* residual, const void* weight, void* y, int dtype,
+                          int M, int H, float eps, void* stream) {
+  if (!x || !weight || !y) return NG_ERR_NULL_POINTER;
+  if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || H < 1) return NG_ERR_BAD_SHAPE;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (dtype == NG_DTYPE_BF16)
+    rmsnorm_kernel<true><<<M, 512, 0, st>>>(x, residual, weight, y, H, eps);
+  else
+    rmsnorm_kernel<false><<<M, 512, 0, st>>>(x, residual, weight, y, H, eps);
+  return launch_status();
+}
+
+extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache,
+                              const int* pos, int dtype, int M, int Hq, int Hkv, int D, float theta,
+                              int max_ctx, void* stream) {
+  if (!qkv || !q_out || !k_cache || !v_cache || !pos) return NG_ERR_NULL_POINTER;
+  if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || Hq < 1 || Hkv < 1 || D < 2 || D % 2 || Hq % Hkv || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  auto st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(Hq + Hkv, M);
+  if (dtype == NG_DTYPE_BF16)
+    rope_append_kernel<true><<<grid, 64, 0, st>>>(qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
+                                                   max_ctx);
+  else
+    rope_append_kernel<false><<<grid, 64, 0, st>>>(qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
+                                                    max_ctx);
+  return launch_status();
+}
+
+extern "C" size_t ng_attn_workspace_bytes(int M, int Hq, int splits) {
+  return static_cast<size_t>(M) * Hq * splits * (2 + kAttnD) * sizeof(float);
+}
+
+extern "C" int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache,
+                              const int* ctx_len, void* out, int dtype, int M, int Hq, int Hkv,
+                              int D, int max_ctx, int splits, float scale, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !ctx_len || !out || !workspace) return NG_ERR_NULL_POINTER;
+  if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
+  if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || Hq / Hkv > 32 || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  if (splits < 1 || splits > 256) return NG_ERR_BAD_ARGUMENT;
+  if (workspace_bytes < ng_attn_workspace_bytes(M, Hq, splits)) return NG_ERR_BAD_ARGUMENT;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int chunk = (max_ctx + splits - 1) / splits;
+  const dim3 g1(Hkv, splits, M), g2(Hq, M);
+  const int threads = (Hq / Hkv) * 32;
+  auto* part = static_cast<float*>(workspace);
+  if (dtype == NG_DTYPE_BF16) {
+    attn_partial_kernel<true><<<g1, threads, 0, st>>>(q, k_cache, v_cache, ctx_len, part, Hq, Hkv,
+                                                      chunk, splits, scale, max_ctx);
+    attn_combine_kernel<true><<<g2, kAttnD, 0, st>>>(part, out, Hq, splits);
+  } else {
+    attn_partial_kernel<false><<<g1, threads, 0, st>>>(q, k_cache, v_cache, ctx_len, part, Hq, Hkv,
+                                                       chunk, splits, scale, max_ctx);
+    attn_combine_kernel<false><<<g2, kAttnD, 0, st>>>(part, out, Hq, splits);
+  }
+  return launch_status();
+}
+
+extern "C" int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int I, void* stream) {
+  if (!gate_up || !out) return NG_ERR_NULL_POINTER;
+  if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || I < 1) return NG_ERR_BAD_SHAPE;
+  auto st = static_cast<cudaStream_t>(stream);
+  const size_t n = static_cast<size_t>(M) * I;
+  const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 148 * 8));
+  if (dtype == NG_DTYPE_BF16)
+    silu_mul_kernel<true><<<blocks, 256, 0, st>>>(gate_up, out, M, I);
+  else
+    silu_mul_kernel<false><<<blocks, 256, 0, st>>>(gate_up, out, M, I);
+  return launch_status();
+}

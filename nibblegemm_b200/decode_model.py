@@ -1,0 +1,204 @@
+"""A full Llama-3-architecture decode step on this library's kernels.
+
+BASELINE config 4/5 asks for tokens/s of a whole decode step: embedding,
+per layer RMSNorm -> q/k/v -> RoPE + KV-cache append -> GQA attention over the
+cache -> o -> residual + RMSNorm -> gate/up -> SwiGLU -> down -> residual, then
+the final norm, the fp16 lm_head and an argmax, captured in one CUDA graph and
+tensor-parallel over the ranks of one node.  The reference's own step is
+projections only (arvindcr4/nibblegemm ``bench/bench_model.py:57-86``); the
+projections here are exactly its W4A16 ops (``gemv_w4a16``), the rest are the
+kernels of ``csrc/decode_ops.cu``.
+
+Layout choices:
+* q|k|v and gate|up are each ONE packed INT4 weight (column concatenation of
+  the projections, per rank), so a layer is four GEMV launches;
+* tensor parallelism is Megatron-style: q/k/v by heads and gate/up by
+  intermediate columns (column-parallel), o and down by rows (row-parallel,
+  followed by an all-reduce -- the peer-memory kernel or NCCL); each rank
+  keeps its KV heads' cache; the lm_head is vocab-parallel and the argmax is
+  combined with one all-gather of (value, index) pairs;
+* weights are random-init (seeded N(0, 0.02)) and quantised round-to-nearest
+  on the device with the reference's RTN rule; every rank draws the same full
+  weights and keeps its shard, so TP = n computes the TP = 1 model.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .ops import extension
+from .quant import QuantizedWeight, quantize_on_device
+
+LLAMA3_8B_MODEL = dict(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128,
+                       intermediate=14336, vocab=128256, rope_theta=500000.0, eps=1e-5)
+LLAMA3_70B_MODEL = dict(layers=80, hidden=8192, heads=64, kv_heads=8, head_dim=128,
+                        intermediate=28672, vocab=128256, rope_theta=500000.0, eps=1e-5)
+
+_DT = {torch.float16: _lib.NG_DTYPE_F16, torch.bfloat16: _lib.NG_DTYPE_BF16}
+
+
+def _cat_cols(ws):
+    return QuantizedWeight(torch.cat([w.qweight for w in ws], 1).contiguous(),
+                           torch.cat([w.scales for w in ws], 1).contiguous(), ws[0].group_size,
+                           ws[0].K, sum(w.N for w in ws))
+
+
+class Llama3Decoder:
+    """Random-init INT4 Llama-3 decoder for batch ``batch`` decode steps.
+
+    ``step()`` advances every sequence by one token (reads ``self.tokens``,
+    writes the argmax token back into it) and is capturable into one CUDA graph;
+    ``self.pos`` (device int32 [batch]) is the position being written.
+    """
+
+    def __init__(self, cfg=LLAMA3_8B_MODEL, batch: int = 1, max_ctx: int = 1024,
+                 layers: Optional[int] = None, rank: int = 0, world: int = 1,
+                 device: Optional[torch.device] = None, seed: int = 0,
+                 dtype: torch.dtype = torch.float16, group_size: int = 128,
+                 reduce: str = "peer", attn_splits: int = 16):
+        self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.layers = layers if layers is not None else cfg["layers"]
+        self.max_ctx, self.attn_splits = max_ctx, attn_splits
+        H, D = cfg["hidden"], cfg["head_dim"]
+        hq, hkv, inter = cfg["heads"] // world, cfg["kv_heads"] // world, cfg["intermediate"] // world
+        if cfg["heads"] % world or cfg["kv_heads"] % world or cfg["intermediate"] % world:
+            raise ValueError(f"{world} ranks do not divide the heads / intermediate size")
+        self.hq, self.hkv, self.inter = hq, hkv, inter
+        self.ext = extension()
+        dev, g = self.device, torch.Generator(device=self.device)
+
+        def dense(K, N, tag):
+            g.manual_seed(seed * 1_000_003 + tag)
+            return torch.randn(K, N, generator=g, device=dev) * 0.02
+
+        def q4(W):
+            return quantize_on_device(W, group_size)
+
+        self.w = []
+        for li in range(self.layers):
+            base = 100 * li
+            wq, wk, wv = q4(dense(H, cfg["heads"] * D, base + 1)), q4(dense(H, cfg["kv_heads"] * D, base + 2)), \
+                q4(dense(H, cfg["kv_heads"] * D, base + 3))
+            qkv = _cat_cols([wq.shard_columns(rank * hq * D, (rank + 1) * hq * D),
+                             wk.shard_columns(rank * hkv * D, (rank + 1) * hkv * D),
+                             wv.shard_columns(rank * hkv * D, (rank + 1) * hkv * D)])
+            del wq, wk, wv
+            wo = q4(dense(cfg["heads"] * D, H, base + 4)).shard_rows(rank * hq * D, (rank + 1) * hq * D)
+            wg = q4(dense(H, cfg["intermediate"], base + 5))
+            wu = q4(dense(H, cfg["intermediate"], base + 6))
+            gu = _cat_cols([wg.shard_columns(rank * inter, (rank + 1) * inter),
+                            wu.shard_columns(rank * inter, (rank + 1) * inter)])
+            del wg, wu
+            wd = q4(dense(cfg["intermediate"], H, base + 7)).shard_rows(rank * inter, (rank + 1) * inter)
+            g.manual_seed(seed * 1_000_003 + base + 8)
+            n1 = (1.0 + 0.1 * torch.randn(H, generator=g, device=dev)).to(dtype)
+            n2 = (1.0 + 0.1 * torch.randn(H, generator=g, device=dev)).to(dtype)
+            self.w.append(dict(qkv=qkv, o=wo, gu=gu, down=wd, attn_norm=n1, mlp_norm=n2))
+        g.manual_seed(seed * 1_000_003 + 99_999)
+        V = cfg["vocab"]
+        self.embed = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(dtype)
+        vl = (V + world - 1) // world
+        self.v0, self.v1 = rank * vl, min(V, (rank + 1) * vl)
+        g.manual_seed(seed * 1_000_003 + 99_998)
+        self.lm_head = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(dtype)[self.v0:self.v1].contiguous()
+        self.final_norm = torch.ones(H, device=dev, dtype=dtype)
+        torch.cuda.synchronize(dev)
+
+        B = batch
+        self.k_cache = [torch.zeros(max_ctx, hkv, D, device=dev, dtype=dtype) for _ in range(self.layers)]
+        self.v_cache = [torch.zeros(max_ctx, hkv, D, device=dev, dtype=dtype) for _ in range(self.layers)]
+        self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.ctx = torch.ones(B, dtype=torch.int32, device=dev)
+        self.res = torch.zeros(B, H, device=dev, dtype=dtype)
+        self.xn = torch.empty(B, H, device=dev, dtype=dtype)
+        self.qkv = torch.empty(B, (hq + 2 * hkv) * D, device=dev, dtype=dtype)
+        self.q = torch.empty(B, hq * D, device=dev, dtype=dtype)
+        self.attn = torch.empty(B, hq * D, device=dev, dtype=dtype)
+        self.o = torch.empty(B, H, device=dev, dtype=dtype)
+        self.gu = torch.empty(B, 2 * inter, device=dev, dtype=dtype)
+        self.act = torch.empty(B, inter, device=dev, dtype=dtype)
+        self.down = torch.empty(B, H, device=dev, dtype=dtype)
+        self.logits = torch.empty(B, self.v1 - self.v0, device=dev, dtype=dtype)
+        self.attn_ws = torch.empty(self.ext.lib.ng_attn_workspace_bytes(B, hq, attn_splits),
+                                   dtype=torch.uint8, device=dev)
+        self._peer = None
+        if world > 1 and reduce == "peer":
+            from .comm import PeerAllReduce
+            self._peer = PeerAllReduce(B * H, device=dev)
+        self.weight_bytes = sum(w[k].weight_bytes for w in self.w for k in ("qkv", "o", "gu", "down"))
+
+    # -- helpers ---------------------------------------------------------------
+    def _stream(self):
+        return torch.cuda.current_stream().cuda_stream
+
+    def _gemv(self, x, w, out):
+        # cluster GEMV (algo 1 / 2): fastest in a mixed chain of shapes
+        self.ext.gemv_w4a16(x, w.qweight, w.scales, w.group_size,
+                            algo=2 if x.dtype == torch.bfloat16 else 1, out=out)
+
+    def _allreduce(self, t):
+        if self.world == 1:
+            return
+        if self._peer is not None:
+            self._peer(t)
+        else:
+            torch.distributed.all_reduce(t)
+
+    def _norm(self, x, res, w, y):
+        _lib.check(self.ext.lib.ng_rmsnorm(x.data_ptr(), res.data_ptr() if res is not None else None,
+                                           w.data_ptr(), y.data_ptr(), _DT[self.dtype], x.size(0),
+                                           x.size(1), float(self.cfg["eps"]), self._stream()),
+                   "rmsnorm")
+
+    # -- the step ----------------------------------------------------------------
+    def step(self, advance: bool = True) -> None:
+        """One token per sequence at position ``self.pos``; ``advance=False``
+        keeps the position (a benchmark holding the context length fixed)."""
+        cfg, D, B = self.cfg, self.cfg["head_dim"], self.batch
+        lib, dt = self.ext.lib, _DT[self.dtype]
+        torch.add(self.pos, 1, out=self.ctx)
+        x = torch.nn.functional.embedding(self.tokens, self.embed)
+        self.res.zero_()
+        delta = x
+        for li, w in enumerate(self.w):
+            self._norm(delta, self.res, w["attn_norm"], self.xn)
+            self._gemv(self.xn, w["qkv"], self.qkv)
+            _lib.check(lib.ng_rope_append(self.qkv.data_ptr(), self.q.data_ptr(),
+                                          self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
+                                          self.pos.data_ptr(), dt, B, self.hq, self.hkv, D,
+                                          float(cfg["rope_theta"]), self.max_ctx, self._stream()),
+                       "rope_append")
+            _lib.check(lib.ng_attn_decode(self.q.data_ptr(), self.k_cache[li].data_ptr(),
+                                          self.v_cache[li].data_ptr(), self.ctx.data_ptr(),
+                                          self.attn.data_ptr(), dt, B, self.hq, self.hkv, D,
+                                          self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D),
+                                          self.attn_ws.data_ptr(), self.attn_ws.numel(),
+                                          self._stream()), "attn_decode")
+            self._gemv(self.attn, w["o"], self.o)
+            self._allreduce(self.o)
+            self._norm(self.o, self.res, w["mlp_norm"], self.xn)
+            self._gemv(self.xn, w["gu"], self.gu)
+            _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
+                                       self._stream()), "silu_mul")
+            self._gemv(self.act, w["down"], self.down)
+            self._allreduce(self.down)
+            delta = self.down
+        self._norm(delta, self.res, self.final_norm, self.xn)
+        torch.mm(self.xn, self.lm_head.t(), out=self.logits)
+        val, idx = self.logits.float().max(dim=1)
+        if self.world > 1:
+            pair = torch.stack([val, (idx + self.v0).float()], 1)  # exact for indices < 2^24
+            allp = [torch.empty_like(pair) for _ in range(self.world)]
+            torch.distributed.all_gather(allp, pair)
+            allp = torch.stack(allp, 0)  # [world, B, 2]
+            best = allp[:, :, 0].argmax(dim=0)
+            self.tokens.copy_(allp[best, torch.arange(B, device=self.device), 1].long())
+        else:
+            self.tokens.copy_(idx)
+        if advance:
+            self.pos.add_(1)

@@ -120,10 +120,19 @@ def quantize(W: torch.Tensor, group_size: int = 128, clip_search: bool = False) 
         raise ValueError(f"K={K} must be divisible by group_size={group_size}")
     if group_size % PACK_FACTOR:
         raise ValueError(f"group_size={group_size} must be divisible by {PACK_FACTOR}")
+    return quantize_on_device(W, group_size).to("cpu")
+
+
+def quantize_on_device(W: torch.Tensor, group_size: int = 128) -> QuantizedWeight:
+    """:func:`quantize` leaving the packed weight on ``W``'s device (the same RTN
+    arithmetic, run by torch on a CUDA tensor: quantising a model's 224
+    projections on the GPU takes seconds)."""
+    K, N = W.shape
+    if K % group_size or group_size % PACK_FACTOR:
+        raise ValueError(f"K={K} / group_size={group_size} not supported")
     w = W.detach().float().reshape(K // group_size, group_size, N)
     scale = (w.abs().amax(dim=1) / QMAX).clamp(min=1e-8)
     codes = (torch.round(w / scale.unsqueeze(1)).clamp(QMIN, QMAX) + ZERO_POINT).reshape(K, N)
-    return QuantizedWeight(
-        qweight=pack_nibbles_torch(codes).cpu().contiguous(),
-        scales=scale.to(torch.float16).cpu().contiguous(),
-        group_size=group_size, K=K, N=N)
+    return QuantizedWeight(qweight=pack_nibbles_torch(codes).contiguous(),
+                           scales=scale.to(torch.float16).contiguous(), group_size=group_size,
+                           K=K, N=N)
