@@ -217,8 +217,8 @@ int ng_ipc_close(void* dev_ptr);
  *     written back to it), y = h * rsqrt(mean(h^2) + eps) * weight.  [M, H].
  *   ng_rope_append: qkv [M, (Hq + 2 Hkv) * D] -> q_out [M, Hq, D] with RoPE
  *     ("rotate half" pairs (i, i + D/2), angle pos * theta^(-2i/D)), K rows
- *     rotated and V rows copied into k_cache / v_cache [max_ctx, Hkv, D] at
- *     row pos[m] (device int array of M positions; rows outside [0, max_ctx)
+ *     rotated and V rows copied into k_cache / v_cache [M, max_ctx, Hkv, D]
+ *     (one cache per sequence) at row pos[m] (device int array of M positions; rows outside [0, max_ctx)
  *     are not written).
  *   ng_attn_decode: GQA attention of q [M, Hq, D] (D = 128) over the first
  *     min(ctx_len[m], max_ctx) cache rows (device int array), softmax scale; the

@@ -61,7 +61,7 @@ __global__ void rmsnorm_kernel(const void* __restrict__ x, void* __restrict__ re
 }
 
 // qkv[M, (Hq + 2 Hkv) * D] -> q[M, Hq, D] with RoPE, and K / V rows of every
-// token appended at its position: cache[pos, Hkv, D].  Rotary pairs (i,
+// token appended at its position in its own sequence's cache: cache[m, pos, Hkv, D].  Rotary pairs (i,
 // i + D/2) ("rotate half"), angle pos * theta^(-2i/D) computed in fp32.
 template <bool BF16>
 __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restrict__ q_out,
@@ -87,7 +87,7 @@ __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restric
       st_act<BF16>(q_out, dst + i + half, rb);
     } else {
       const int kh = head - Hq;
-      const size_t dst = (static_cast<size_t>(p) * Hkv + kh) * D;
+      const size_t dst = ((static_cast<size_t>(m) * max_ctx + p) * Hkv + kh) * D;
       st_act<BF16>(k_cache, dst + i, ra);
       st_act<BF16>(k_cache, dst + i + half, rb);
     }
@@ -95,7 +95,7 @@ __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restric
   if (head >= Hq) {  // V rows: copied unrotated
     const int kh = head - Hq;
     const size_t vsrc = static_cast<size_t>(m) * row + static_cast<size_t>(Hq + Hkv + kh) * D;
-    const size_t dst = (static_cast<size_t>(p) * Hkv + kh) * D;
+    const size_t dst = ((static_cast<size_t>(m) * max_ctx + p) * Hkv + kh) * D;
     for (int i = threadIdx.x; i < D; i += blockDim.x)
       static_cast<unsigned short*>(v_cache)[dst + i] = static_cast<const unsigned short*>(qkv)[vsrc + i];
   }
@@ -124,7 +124,7 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
   for (int j = 0; j < 4; ++j) qv[j] = ld_act<BF16>(q, qb + j) * scale;
   float mx = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int t = t0; t < t1; ++t) {
-    const size_t kb = (static_cast<size_t>(t) * Hkv + kh) * kAttnD + lane * 4;
+    const size_t kb = ((static_cast<size_t>(m) * max_ctx + t) * Hkv + kh) * kAttnD + lane * 4;
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) s += qv[j] * ld_act<BF16>(k_cache, kb + j);

@@ -109,8 +109,9 @@ class Llama3Decoder:
         torch.cuda.synchronize(dev)
 
         B = batch
-        self.k_cache = [torch.zeros(max_ctx, hkv, D, device=dev, dtype=dtype) for _ in range(self.layers)]
-        self.v_cache = [torch.zeros(max_ctx, hkv, D, device=dev, dtype=dtype) for _ in range(self.layers)]
+        # one cache per sequence: [batch, max_ctx, kv heads, head_dim] per layer
+        self.k_cache = [torch.zeros(B, max_ctx, hkv, D, device=dev, dtype=dtype) for _ in range(self.layers)]
+        self.v_cache = [torch.zeros(B, max_ctx, hkv, D, device=dev, dtype=dtype) for _ in range(self.layers)]
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.ctx = torch.ones(B, dtype=torch.int32, device=dev)

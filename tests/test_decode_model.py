@@ -45,7 +45,7 @@ class RefModel:
         self.m, c = m, m.cfg
         self.W = [{k: _deq(w[k]) for k in ("qkv", "o", "gu", "down")} | {"n1": w["attn_norm"], "n2": w["mlp_norm"]}
                   for w in m.w]
-        self.kc = [torch.zeros(m.max_ctx, c["kv_heads"], c["head_dim"], device=m.device) for _ in m.w]
+        self.kc = [torch.zeros(m.batch, m.max_ctx, c["kv_heads"], c["head_dim"], device=m.device) for _ in m.w]
         self.vc = [torch.zeros_like(k) for k in self.kc]
 
     def step(self, tokens, pos):
@@ -63,8 +63,8 @@ class RefModel:
             out = torch.empty(tokens.numel(), hq, D, device=m.device)
             for b in range(tokens.numel()):
                 p = int(pos[b])
-                self.kc[li][p], self.vc[li][p] = k[b], v[b]
-                K, V = self.kc[li][:p + 1], self.vc[li][:p + 1]  # [T, hkv, D]
+                self.kc[li][b, p], self.vc[li][b, p] = k[b], v[b]
+                K, V = self.kc[li][b, :p + 1], self.vc[li][b, :p + 1]  # [T, hkv, D]
                 for h in range(hq):
                     kh = h // (hq // hkv)
                     s = (K[:, kh] @ q[b, h]) / math.sqrt(D)
