@@ -19,6 +19,23 @@ __device__ __forceinline__ float ld_act(const void* p, size_t i) {
   const unsigned short v = static_cast<const unsigned short*>(p)[i];
   return BF16 ? __uint_as_float(static_cast<uint32_t>(v) << 16) : __half2float(__ushort_as_half(v));
 }
+// Four consecutive activations (8 bytes, 8-byte aligned) as fp32.
+template <bool BF16>
+__device__ __forceinline__ void ld_act4(const void* p, size_t i, float (&f)[4]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const unsigned short*>(p) + i);
+  const uint32_t w[2] = {v.x, v.y};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    if constexpr (BF16) {
+      f[2 * j] = __uint_as_float(w[j] << 16);
+      f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    } else {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+}
 template <bool BF16>
 __device__ __forceinline__ void st_act(void* p, size_t i, float v) {
   static_cast<unsigned short*>(p)[i] =
@@ -125,15 +142,18 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
   float mx = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int t = t0; t < t1; ++t) {
     const size_t kb = ((static_cast<size_t>(m) * max_ctx + t) * Hkv + kh) * kAttnD + lane * 4;
+    float kv4[4], vv4[4];
+    ld_act4<BF16>(k_cache, kb, kv4);
+    ld_act4<BF16>(v_cache, kb, vv4);
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s += qv[j] * ld_act<BF16>(k_cache, kb + j);
+    for (int j = 0; j < 4; ++j) s += qv[j] * kv4[j];
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float nm = fmaxf(mx, s);
     const float corr = __expf(mx - nm), pw = __expf(s - nm);
     sum = sum * corr + pw;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * ld_act<BF16>(v_cache, kb + j);
+    for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * vv4[j];
     mx = nm;
   }
   // part layout: [M][Hq][splits][2 + D]
