@@ -42,6 +42,14 @@ __device__ __forceinline__ void st_act(void* p, size_t i, float v) {
       BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
 }
 
+// Programmatic dependent launch: let the next kernel on the stream launch
+// now (a following GEMV starts streaming its weights), then wait for the
+// producer of this kernel's inputs.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -58,6 +66,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 template <bool BF16>
 __global__ void rmsnorm_kernel(const void* __restrict__ x, void* __restrict__ residual,
                                const void* __restrict__ w, void* __restrict__ y, int H, float eps) {
+  pdl_enter();
   __shared__ float red[32];
   const size_t base = static_cast<size_t>(blockIdx.x) * H;
   float ss = 0.f;
@@ -85,6 +94,7 @@ __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restric
                                    void* __restrict__ k_cache, void* __restrict__ v_cache,
                                    const int* __restrict__ pos, int Hq, int Hkv, int D, float theta,
                                    int max_ctx) {
+  pdl_enter();
   const int m = blockIdx.y, head = blockIdx.x;  // head in [0, Hq + Hkv): q heads then k heads
   const int p = pos[m];
   const bool in_cache = p >= 0 && p < max_ctx;  // cache rows outside [0, max_ctx) are never written
@@ -129,6 +139,7 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
                                     const void* __restrict__ v_cache, const int* __restrict__ ctx,
                                     float* __restrict__ part, int Hq, int Hkv, int chunk,
                                     int splits, float scale, int max_ctx) {
+  pdl_enter();
   const int kh = blockIdx.x, sp = blockIdx.y, m = blockIdx.z;
   const int G = Hq / Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -170,6 +181,7 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
 template <bool BF16>
 __global__ void attn_combine_kernel(const float* __restrict__ part, void* __restrict__ out,
                                     int Hq, int splits) {
+  pdl_enter();
   const int qh = blockIdx.x, m = blockIdx.y, d = threadIdx.x;  // blockDim = D
   const float* p = part + (static_cast<size_t>(m) * Hq + qh) * splits * (2 + kAttnD);
   float mx = -INFINITY;
@@ -188,6 +200,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, void* __rest
 // gate_up[M, 2I] (gate | up) -> out[M, I] = silu(gate) * up.
 template <bool BF16>
 __global__ void silu_mul_kernel(const void* __restrict__ gu, void* __restrict__ out, int M, int I) {
+  pdl_enter();
   const size_t n = static_cast<size_t>(M) * I;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -198,6 +211,21 @@ __global__ void silu_mul_kernel(const void* __restrict__ gu, void* __restrict__ 
 }
 
 bool dtype_ok(int d) { return d == NG_DTYPE_F16 || d == NG_DTYPE_BF16; }
+
+// Launch with programmatic stream serialisation (see pdl_enter).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+}
 
 }  // namespace
 }  // namespace ngb
@@ -211,10 +239,9 @@ extern "C" int ng_rmsnorm(const void* x, void* residual, const void* weight, voi
   if (M < 1 || H < 1) return NG_ERR_BAD_SHAPE;
   auto st = static_cast<cudaStream_t>(stream);
   if (dtype == NG_DTYPE_BF16)
-    rmsnorm_kernel<true><<<M, 512, 0, st>>>(x, residual, weight, y, H, eps);
+    return launch_pdl(rmsnorm_kernel<true>, dim3(M), dim3(512), st, x, residual, weight, y, H, eps);
   else
-    rmsnorm_kernel<false><<<M, 512, 0, st>>>(x, residual, weight, y, H, eps);
-  return launch_status();
+    return launch_pdl(rmsnorm_kernel<false>, dim3(M), dim3(512), st, x, residual, weight, y, H, eps);
 }
 
 extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache,
@@ -226,10 +253,10 @@ extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void*
   auto st = static_cast<cudaStream_t>(stream);
   const dim3 grid(Hq + Hkv, M);
   if (dtype == NG_DTYPE_BF16)
-    rope_append_kernel<true><<<grid, 64, 0, st>>>(qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
+    return launch_pdl(rope_append_kernel<true>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
                                                    max_ctx);
   else
-    rope_append_kernel<false><<<grid, 64, 0, st>>>(qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
+    return launch_pdl(rope_append_kernel<false>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
                                                     max_ctx);
   return launch_status();
 }
@@ -253,15 +280,15 @@ extern "C" int ng_attn_decode(const void* q, const void* k_cache, const void* v_
   const int threads = (Hq / Hkv) * 32;
   auto* part = static_cast<float*>(workspace);
   if (dtype == NG_DTYPE_BF16) {
-    attn_partial_kernel<true><<<g1, threads, 0, st>>>(q, k_cache, v_cache, ctx_len, part, Hq, Hkv,
-                                                      chunk, splits, scale, max_ctx);
-    attn_combine_kernel<true><<<g2, kAttnD, 0, st>>>(part, out, Hq, splits);
-  } else {
-    attn_partial_kernel<false><<<g1, threads, 0, st>>>(q, k_cache, v_cache, ctx_len, part, Hq, Hkv,
-                                                       chunk, splits, scale, max_ctx);
-    attn_combine_kernel<false><<<g2, kAttnD, 0, st>>>(part, out, Hq, splits);
+    if (int e = launch_pdl(attn_partial_kernel<true>, g1, dim3(threads), st, q, k_cache, v_cache,
+                           ctx_len, part, Hq, Hkv, chunk, splits, scale, max_ctx))
+      return e;
+    return launch_pdl(attn_combine_kernel<true>, g2, dim3(kAttnD), st, part, out, Hq, splits);
   }
-  return launch_status();
+  if (int e = launch_pdl(attn_partial_kernel<false>, g1, dim3(threads), st, q, k_cache, v_cache,
+                         ctx_len, part, Hq, Hkv, chunk, splits, scale, max_ctx))
+    return e;
+  return launch_pdl(attn_combine_kernel<false>, g2, dim3(kAttnD), st, part, out, Hq, splits);
 }
 
 extern "C" int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int I, void* stream) {
@@ -272,8 +299,8 @@ extern "C" int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int
   const size_t n = static_cast<size_t>(M) * I;
   const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 148 * 8));
   if (dtype == NG_DTYPE_BF16)
-    silu_mul_kernel<true><<<blocks, 256, 0, st>>>(gate_up, out, M, I);
+    return launch_pdl(silu_mul_kernel<true>, dim3(blocks), dim3(256), st, gate_up, out, M, I);
   else
-    silu_mul_kernel<false><<<blocks, 256, 0, st>>>(gate_up, out, M, I);
+    return launch_pdl(silu_mul_kernel<false>, dim3(blocks), dim3(256), st, gate_up, out, M, I);
   return launch_status();
 }
