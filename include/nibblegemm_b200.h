@@ -214,7 +214,8 @@ int ng_ipc_close(void* dev_ptr);
  * take fp16 or bf16 activations (`dtype`), compute in fp32, enqueue on
  * `stream` and allocate nothing.
  *   ng_rmsnorm: per token h = x + residual (residual may be NULL; else h is
- *     written back to it), y = h * rsqrt(mean(h^2) + eps) * weight.  [M, H].
+ *     written back to it), y = h * rsqrt(mean(h^2) + eps) * weight.  [M, H],
+ *     H <= 8192.
  *   ng_rope_append: qkv [M, (Hq + 2 Hkv) * D] -> q_out [M, Hq, D] with RoPE
  *     ("rotate half" pairs (i, i + D/2), angle pos * theta^(-2i/D)), K rows
  *     rotated and V rows copied into k_cache / v_cache [M, max_ctx, Hkv, D]
@@ -236,6 +237,12 @@ int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache, cons
                    void* out, int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,
                    float scale, void* workspace, size_t workspace_bytes, void* stream);
 int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int I, void* stream);
+/* Row-wise argmax of logits [M, V] (ties: smallest index): value[m] (fp32) and
+ * index[m] + index_offset (int64; the offset places a vocab shard).
+ * best_scratch: M x 8 bytes, zero before the first call; each call leaves it
+ * at zero.  Calls sharing it must not overlap on the GPU. */
+int ng_argmax(const void* logits, int dtype, int M, int V, long long index_offset,
+              void* best_scratch, float* value, long long* index, void* stream);
 
 #ifdef __cplusplus
 }

@@ -63,26 +63,36 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // h = x + residual (if residual != null; h is written back to residual),
 // y = h * rsqrt(mean(h^2) + eps) * w.  One CTA per token.
+constexpr int kNormThreads = 512;
+constexpr int kNormMaxPer = 16;  // H <= 8192 elements per token held in registers
+
 template <bool BF16>
-__global__ void rmsnorm_kernel(const void* __restrict__ x, void* __restrict__ residual,
-                               const void* __restrict__ w, void* __restrict__ y, int H, float eps) {
+__global__ void __launch_bounds__(kNormThreads)
+    rmsnorm_kernel(const void* __restrict__ x, void* __restrict__ residual,
+                   const void* __restrict__ w, void* __restrict__ y, int H, float eps) {
   pdl_enter();
   __shared__ float red[32];
   const size_t base = static_cast<size_t>(blockIdx.x) * H;
+  float h[kNormMaxPer];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float h = ld_act<BF16>(x, base + i);
-    if (residual) h += ld_act<BF16>(residual, base + i);
-    ss += h * h;
+#pragma unroll
+  for (int j = 0; j < kNormMaxPer; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    h[j] = 0.f;
+    if (i < H) {
+      h[j] = ld_act<BF16>(x, base + i);
+      if (residual) h[j] += ld_act<BF16>(residual, base + i);
+      ss += h[j] * h[j];
+    }
   }
   const float inv = rsqrtf(block_sum(ss, red) / static_cast<float>(H) + eps);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float h = ld_act<BF16>(x, base + i);
-    if (residual) {
-      h += ld_act<BF16>(residual, base + i);
-      st_act<BF16>(residual, base + i, h);
+#pragma unroll
+  for (int j = 0; j < kNormMaxPer; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    if (i < H) {
+      if (residual) st_act<BF16>(residual, base + i, h[j]);
+      st_act<BF16>(y, base + i, h[j] * inv * ld_act<BF16>(w, i));
     }
-    st_act<BF16>(y, base + i, h * inv * ld_act<BF16>(w, i));
   }
 }
 
@@ -151,21 +161,37 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
 #pragma unroll
   for (int j = 0; j < 4; ++j) qv[j] = ld_act<BF16>(q, qb + j) * scale;
   float mx = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int t = t0; t < t1; ++t) {
-    const size_t kb = ((static_cast<size_t>(m) * max_ctx + t) * Hkv + kh) * kAttnD + lane * 4;
-    float kv4[4], vv4[4];
-    ld_act4<BF16>(k_cache, kb, kv4);
-    ld_act4<BF16>(v_cache, kb, vv4);
-    float s = 0.f;
+  constexpr int kB = 8;  // positions whose K / V rows are loaded together
+  for (int tb = t0; tb < t1; tb += kB) {
+    float kv[kB][4], vv[kB][4], sc[kB];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s += qv[j] * kv4[j];
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float nm = fmaxf(mx, s);
-    const float corr = __expf(mx - nm), pw = __expf(s - nm);
-    sum = sum * corr + pw;
+    for (int u = 0; u < kB; ++u) {
+      if (tb + u < t1) {
+        const size_t kb = ((static_cast<size_t>(m) * max_ctx + tb + u) * Hkv + kh) * kAttnD + lane * 4;
+        ld_act4<BF16>(k_cache, kb, kv[u]);
+        ld_act4<BF16>(v_cache, kb, vv[u]);
+      }
+    }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * vv4[j];
-    mx = nm;
+    for (int u = 0; u < kB; ++u) {
+      sc[u] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[u] += qv[j] * kv[u][j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < kB; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      if (tb + u >= t1) break;
+      const float nm = fmaxf(mx, sc[u]);
+      const float corr = __expf(mx - nm), pw = __expf(sc[u] - nm);
+      sum = sum * corr + pw;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * vv[u][j];
+      mx = nm;
+    }
   }
   // part layout: [M][Hq][splits][2 + D]
   float* o = part + ((static_cast<size_t>(m) * Hq + qh) * splits + sp) * (2 + kAttnD);
@@ -210,6 +236,47 @@ __global__ void silu_mul_kernel(const void* __restrict__ gu, void* __restrict__ 
   }
 }
 
+// Row-wise argmax of logits [M, V]: every block folds a strided slice of
+// the row into one (value, index) key -- float bits mapped to an unsigned
+// order, index complemented so the smallest index wins ties -- and takes
+// atomicMax into best[m]; the order of the atomics cannot change the result.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(i));
+}
+
+template <bool BF16>
+__global__ void argmax_partial_kernel(const void* __restrict__ logits, int V,
+                                      unsigned long long* __restrict__ best) {
+  pdl_enter();
+  const int m = blockIdx.y;
+  unsigned long long k = 0ull;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+    const unsigned long long c = argmax_key(ld_act<BF16>(logits, static_cast<size_t>(m) * V + i), i);
+    k = c > k ? c : k;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
+    k = c > k ? c : k;
+  }
+  if ((threadIdx.x & 31) == 0 && k) atomicMax(&best[m], k);
+}
+
+// best[m] -> (value, index + offset); best[m] re-armed to 0 for the next call.
+__global__ void argmax_final_kernel(unsigned long long* __restrict__ best, float* __restrict__ value,
+                                    long long* __restrict__ index, int M, long long offset) {
+  pdl_enter();
+  const int m = threadIdx.x;
+  if (m >= M) return;
+  const unsigned long long k = best[m];
+  uint32_t b = static_cast<uint32_t>(k >> 32);
+  b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
+  value[m] = __uint_as_float(b);
+  index[m] = static_cast<long long>(~static_cast<uint32_t>(k)) + offset;
+  best[m] = 0ull;
+}
+
 bool dtype_ok(int d) { return d == NG_DTYPE_F16 || d == NG_DTYPE_BF16; }
 
 // Launch with programmatic stream serialisation (see pdl_enter).
@@ -236,12 +303,12 @@ extern "C" int ng_rmsnorm(const void* x, void* residual, const void* weight, voi
                           int M, int H, float eps, void* stream) {
   if (!x || !weight || !y) return NG_ERR_NULL_POINTER;
   if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
-  if (M < 1 || H < 1) return NG_ERR_BAD_SHAPE;
+  if (M < 1 || H < 1 || H > kNormThreads * kNormMaxPer) return NG_ERR_BAD_SHAPE;
   auto st = static_cast<cudaStream_t>(stream);
   if (dtype == NG_DTYPE_BF16)
-    return launch_pdl(rmsnorm_kernel<true>, dim3(M), dim3(512), st, x, residual, weight, y, H, eps);
+    return launch_pdl(rmsnorm_kernel<true>, dim3(M), dim3(kNormThreads), st, x, residual, weight, y, H, eps);
   else
-    return launch_pdl(rmsnorm_kernel<false>, dim3(M), dim3(512), st, x, residual, weight, y, H, eps);
+    return launch_pdl(rmsnorm_kernel<false>, dim3(M), dim3(kNormThreads), st, x, residual, weight, y, H, eps);
 }
 
 extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache,
@@ -303,4 +370,20 @@ extern "C" int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int
   else
     return launch_pdl(silu_mul_kernel<false>, dim3(blocks), dim3(256), st, gate_up, out, M, I);
   return launch_status();
+}
+
+extern "C" int ng_argmax(const void* logits, int dtype, int M, int V, long long index_offset,
+                         void* best_scratch, float* value, long long* index, void* stream) {
+  if (!logits || !best_scratch || !value || !index) return NG_ERR_NULL_POINTER;
+  if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 1024 || V < 1) return NG_ERR_BAD_SHAPE;
+  auto st = static_cast<cudaStream_t>(stream);
+  auto* best = static_cast<unsigned long long*>(best_scratch);
+  const int blocks = std::max(1, std::min(148, (V + 255) / 256));
+  const dim3 grid(blocks, M);
+  int e = dtype == NG_DTYPE_BF16 ? launch_pdl(argmax_partial_kernel<true>, grid, dim3(256), st, logits, V, best)
+                                 : launch_pdl(argmax_partial_kernel<false>, grid, dim3(256), st, logits, V, best);
+  if (e) return e;
+  return launch_pdl(argmax_final_kernel, dim3(1), dim3(std::max(32, (M + 31) / 32 * 32)), st, best, value,
+                    index, M, index_offset);
 }

@@ -58,7 +58,7 @@ class Llama3Decoder:
                  layers: Optional[int] = None, rank: int = 0, world: int = 1,
                  device: Optional[torch.device] = None, seed: int = 0,
                  dtype: torch.dtype = torch.float16, group_size: int = 128,
-                 reduce: str = "peer", attn_splits: int = 16):
+                 reduce: str = "peer", attn_splits: int = 32):
         self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
@@ -125,6 +125,9 @@ class Llama3Decoder:
         self.act = torch.empty(B, inter, device=dev, dtype=dtype)
         self.down = torch.empty(B, H, device=dev, dtype=dtype)
         self.logits = torch.empty(B, self.v1 - self.v0, device=dev, dtype=dtype)
+        self.best_scratch = torch.zeros(B, dtype=torch.int64, device=dev)  # argmax keys, re-armed per call
+        self.best_val = torch.empty(B, dtype=torch.float32, device=dev)
+        self.best_idx = torch.empty(B, dtype=torch.int64, device=dev)
         self.attn_ws = torch.empty(self.ext.lib.ng_attn_workspace_bytes(B, hq, attn_splits),
                                    dtype=torch.uint8, device=dev)
         self._peer = None
@@ -191,15 +194,16 @@ class Llama3Decoder:
             delta = self.down
         self._norm(delta, self.res, self.final_norm, self.xn)
         torch.mm(self.xn, self.lm_head.t(), out=self.logits)
-        val, idx = self.logits.float().max(dim=1)
+        idx_out = self.tokens if self.world == 1 else self.best_idx
+        _lib.check(self.ext.lib.ng_argmax(self.logits.data_ptr(), _DT[self.dtype], B, self.v1 - self.v0,
+                                          self.v0, self.best_scratch.data_ptr(), self.best_val.data_ptr(),
+                                          idx_out.data_ptr(), self._stream()), "argmax")
         if self.world > 1:
-            pair = torch.stack([val, (idx + self.v0).float()], 1)  # exact for indices < 2^24
+            pair = torch.stack([self.best_val, self.best_idx.float()], 1)  # exact for indices < 2^24
             allp = [torch.empty_like(pair) for _ in range(self.world)]
             torch.distributed.all_gather(allp, pair)
             allp = torch.stack(allp, 0)  # [world, B, 2]
             best = allp[:, :, 0].argmax(dim=0)
             self.tokens.copy_(allp[best, torch.arange(B, device=self.device), 1].long())
-        else:
-            self.tokens.copy_(idx)
         if advance:
             self.pos.add_(1)

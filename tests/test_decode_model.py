@@ -172,3 +172,23 @@ def test_decoder_tp2_generates_the_tp1_tokens():
         p.join(timeout=60)
     assert "worker error" not in res, res
     assert res["tp"] == res["tp1"]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,V", [(1, 128256), (3, 1000), (5, 7)])
+def test_argmax_kernel_matches_torch_and_rearms(dtype, M, V):
+    ext = ng.extension()
+    scratch = torch.zeros(M, dtype=torch.int64, device="cuda")
+    for trial in range(3):
+        x = torch.randn(M, V, generator=torch.Generator().manual_seed(trial)).to(dtype).cuda()
+        x[:, V // 2] = x.max() if trial == 2 else x[:, V // 2]  # a tie on the last trial
+        val = torch.empty(M, dtype=torch.float32, device="cuda")
+        idx = torch.empty(M, dtype=torch.int64, device="cuda")
+        st = ext.lib.ng_argmax(x.data_ptr(), 1 if dtype == torch.bfloat16 else 0, M, V, 100,
+                               scratch.data_ptr(), val.data_ptr(), idx.data_ptr(),
+                               torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+        torch.cuda.synchronize()
+        ref_v, ref_i = x.float().max(dim=1)  # torch returns the first maximal index
+        assert torch.equal(idx - 100, ref_i) and torch.equal(val, ref_v)
+        assert int(scratch.count_nonzero()) == 0
