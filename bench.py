@@ -290,7 +290,7 @@ def run_decode(args, wl, world, rank, local, dist):
     """Tokens/s of the full Llama-3-8B decode step.
 
     One step = one token through embedding, 32 layers (RMSNorm, fused q|k|v
-    GEMV, RoPE + KV append, GQA attention over 1024 cached positions, o GEMV,
+    GEMV, GQA attention with RoPE + KV append over 1024 cached positions, o GEMV,
     all-reduce, RMSNorm, fused gate|up GEMV, SwiGLU, down GEMV, all-reduce),
     final norm, fp16 lm_head and argmax; captured once in a CUDA graph and
     replayed with the position held at 1023 (context 1024).  Strong scaling.
@@ -358,8 +358,9 @@ def run_decode(args, wl, world, rank, local, dist):
         kv = 2 * cfg["layers"] * 1024 * m.hkv * cfg["head_dim"] * 2
         nbytes = m.weight_bytes + m.lm_head.numel() * 2 + kv + cfg["hidden"] * 2
         achieved = nbytes / (per_ms * 1e-3) / 1e9
-        # ours per layer: 2 norms, 4 GEMVs, RoPE, 2 attention, SwiGLU (+2 peer all-reduces); final norm
-        launches = 32 * 10 + 1 + (64 if (world > 1 and args.reduce == "peer") else 0)
+        # ours per layer: 2 norms, 4 GEMVs, 2 attention (RoPE + KV append folded in), SwiGLU
+        # (+2 peer all-reduces); then the final norm and 2 argmax kernels
+        launches = 32 * 9 + 3 + (64 if (world > 1 and args.reduce == "peer") else 0)
         line = {
             "metric": METRIC, "value": round(1000.0 / per_ms, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),

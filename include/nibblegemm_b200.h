@@ -236,6 +236,14 @@ size_t ng_attn_workspace_bytes(int M, int Hq, int splits);
 int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int* ctx_len,
                    void* out, int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,
                    float scale, void* workspace, size_t workspace_bytes, void* stream);
+/* ng_rope_append + ng_attn_decode in one pass over the cache: q / K / V are
+ * read from qkv [M, (Hq + 2 Hkv) * D], the new K / V row is written at pos[m]
+ * (if inside the cache) by the chunk that reads it, and the context is
+ * min(pos[m] + 1, max_ctx) rows. */
+int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache, const int* pos, void* out,
+                        int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,
+                        float scale, float theta, void* workspace, size_t workspace_bytes,
+                        void* stream);
 int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int I, void* stream);
 /* Row-wise argmax of logits [M, V] (ties: smallest index): value[m] (fp32) and
  * index[m] + index_offset (int64; the offset places a vocab shard).

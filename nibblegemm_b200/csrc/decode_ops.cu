@@ -203,6 +203,103 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
   for (int j = 0; j < 4; ++j) o[2 + lane * 4 + j] = acc[j];
 }
 
+// attn_partial_kernel with RoPE and the KV append folded in: q is read from
+// qkv [M, (Hq + 2 Hkv) * D] and rotated in registers (the rotation partner of
+// lane l's dims 4l..4l+3 is lane l ^ 16); the CTA whose chunk holds the new
+// position rotates K, writes K and V there, and only then reads the chunk.
+// The context is pos[m] + 1 positions, clamped to the cache.
+template <bool BF16>
+__global__ void attn_rope_partial_kernel(const void* __restrict__ qkv, void* __restrict__ k_cache,
+                                         void* __restrict__ v_cache, const int* __restrict__ pos,
+                                         float* __restrict__ part, int Hq, int Hkv, int chunk,
+                                         int splits, float scale, int max_ctx, float theta) {
+  pdl_enter();
+  const int kh = blockIdx.x, sp = blockIdx.y, m = blockIdx.z;
+  const int G = Hq / Hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qh = kh * G + warp;
+  const int p = pos[m];
+  const int len = min(p + 1, max_ctx);
+  const int t0 = sp * chunk, t1 = min(len, t0 + chunk);
+  const size_t row = static_cast<size_t>(Hq + 2 * Hkv) * kAttnD;
+  // rotation of the 4 dims this lane holds: dims d = 4 lane + j pair with d +- 64
+  const bool lo = lane < 16;
+  float cs[4], sn[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = (lo ? 4 * lane : 4 * lane - kAttnD / 2) + j;  // frequency index 0..63
+    const float inv_freq = exp2f(-2.f * i / kAttnD * log2f(theta));
+    sincosf(static_cast<float>(p) * inv_freq, &sn[j], &cs[j]);
+  }
+  auto rotate = [&](float (&v)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, v[j], 16);
+      v[j] = lo ? v[j] * cs[j] - partner * sn[j] : v[j] * cs[j] + partner * sn[j];
+    }
+  };
+  float qv[4];
+  ld_act4<BF16>(qkv, static_cast<size_t>(m) * row + static_cast<size_t>(qh) * kAttnD + lane * 4, qv);
+  rotate(qv);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qv[j] *= scale;
+  if (p >= 0 && p < max_ctx && p >= t0 && p < t1) {  // this chunk holds the new row: append it
+    if (warp == 0) {
+      float kn[4], vn[4];
+      ld_act4<BF16>(qkv, static_cast<size_t>(m) * row + static_cast<size_t>(Hq + kh) * kAttnD + lane * 4, kn);
+      ld_act4<BF16>(qkv, static_cast<size_t>(m) * row + static_cast<size_t>(Hq + Hkv + kh) * kAttnD + lane * 4, vn);
+      rotate(kn);
+      const size_t dst = ((static_cast<size_t>(m) * max_ctx + p) * Hkv + kh) * kAttnD + lane * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        st_act<BF16>(k_cache, dst + j, kn[j]);
+        st_act<BF16>(v_cache, dst + j, vn[j]);
+      }
+    }
+    __syncthreads();
+  }
+  float mx = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int kB = 8;
+  for (int tb = t0; tb < t1; tb += kB) {
+    float kv[kB][4], vv[kB][4], sc[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      if (tb + u < t1) {
+        const size_t kb = ((static_cast<size_t>(m) * max_ctx + tb + u) * Hkv + kh) * kAttnD + lane * 4;
+        ld_act4<BF16>(k_cache, kb, kv[u]);
+        ld_act4<BF16>(v_cache, kb, vv[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      sc[u] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[u] += qv[j] * kv[u][j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < kB; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      if (tb + u >= t1) break;
+      const float nm = fmaxf(mx, sc[u]);
+      const float corr = __expf(mx - nm), pw = __expf(sc[u] - nm);
+      sum = sum * corr + pw;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * vv[u][j];
+      mx = nm;
+    }
+  }
+  float* o = part + ((static_cast<size_t>(m) * Hq + qh) * splits + sp) * (2 + kAttnD);
+  if (lane == 0) {
+    o[0] = mx;
+    o[1] = sum;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[2 + lane * 4 + j] = acc[j];
+}
+
 // Combine the splits of one (token, q head) in split order: out[M, Hq, D].
 template <bool BF16>
 __global__ void attn_combine_kernel(const float* __restrict__ part, void* __restrict__ out,
@@ -386,4 +483,30 @@ extern "C" int ng_argmax(const void* logits, int dtype, int M, int V, long long 
   if (e) return e;
   return launch_pdl(argmax_final_kernel, dim3(1), dim3(std::max(32, (M + 31) / 32 * 32)), st, best, value,
                     index, M, index_offset);
+}
+
+extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache, const int* pos,
+                                   void* out, int dtype, int M, int Hq, int Hkv, int D, int max_ctx,
+                                   int splits, float scale, float theta, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  if (!qkv || !k_cache || !v_cache || !pos || !out || !workspace) return NG_ERR_NULL_POINTER;
+  if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
+  if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || Hq / Hkv > 32 || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  if (splits < 1 || splits > 256) return NG_ERR_BAD_ARGUMENT;
+  if (workspace_bytes < ng_attn_workspace_bytes(M, Hq, splits)) return NG_ERR_BAD_ARGUMENT;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int chunk = (max_ctx + splits - 1) / splits;
+  const dim3 g1(Hkv, splits, M), g2(Hq, M);
+  const int threads = (Hq / Hkv) * 32;
+  auto* part = static_cast<float*>(workspace);
+  if (dtype == NG_DTYPE_BF16) {
+    if (int e = launch_pdl(attn_rope_partial_kernel<true>, g1, dim3(threads), st, qkv, k_cache, v_cache,
+                           pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta))
+      return e;
+    return launch_pdl(attn_combine_kernel<true>, g2, dim3(kAttnD), st, part, out, Hq, splits);
+  }
+  if (int e = launch_pdl(attn_rope_partial_kernel<false>, g1, dim3(threads), st, qkv, k_cache, v_cache,
+                         pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta))
+    return e;
+  return launch_pdl(attn_combine_kernel<false>, g2, dim3(kAttnD), st, part, out, Hq, splits);
 }

@@ -58,11 +58,11 @@ class Llama3Decoder:
                  layers: Optional[int] = None, rank: int = 0, world: int = 1,
                  device: Optional[torch.device] = None, seed: int = 0,
                  dtype: torch.dtype = torch.float16, group_size: int = 128,
-                 reduce: str = "peer", attn_splits: int = 32):
+                 reduce: str = "peer", attn_splits: int = 32, fused_rope: bool = True):
         self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
-        self.max_ctx, self.attn_splits = max_ctx, attn_splits
+        self.max_ctx, self.attn_splits, self.fused_rope = max_ctx, attn_splits, fused_rope
         H, D = cfg["hidden"], cfg["head_dim"]
         hq, hkv, inter = cfg["heads"] // world, cfg["kv_heads"] // world, cfg["intermediate"] // world
         if cfg["heads"] % world or cfg["kv_heads"] % world or cfg["intermediate"] % world:
@@ -172,17 +172,24 @@ class Llama3Decoder:
         for li, w in enumerate(self.w):
             self._norm(delta, self.res, w["attn_norm"], self.xn)
             self._gemv(self.xn, w["qkv"], self.qkv)
-            _lib.check(lib.ng_rope_append(self.qkv.data_ptr(), self.q.data_ptr(),
-                                          self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
-                                          self.pos.data_ptr(), dt, B, self.hq, self.hkv, D,
-                                          float(cfg["rope_theta"]), self.max_ctx, self._stream()),
-                       "rope_append")
-            _lib.check(lib.ng_attn_decode(self.q.data_ptr(), self.k_cache[li].data_ptr(),
-                                          self.v_cache[li].data_ptr(), self.ctx.data_ptr(),
-                                          self.attn.data_ptr(), dt, B, self.hq, self.hkv, D,
-                                          self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D),
-                                          self.attn_ws.data_ptr(), self.attn_ws.numel(),
-                                          self._stream()), "attn_decode")
+            if self.fused_rope:  # RoPE + KV append inside the attention kernel
+                _lib.check(lib.ng_attn_decode_rope(
+                    self.qkv.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
+                    self.pos.data_ptr(), self.attn.data_ptr(), dt, B, self.hq, self.hkv, D,
+                    self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D), float(cfg["rope_theta"]),
+                    self.attn_ws.data_ptr(), self.attn_ws.numel(), self._stream()), "attn_decode_rope")
+            else:
+                _lib.check(lib.ng_rope_append(self.qkv.data_ptr(), self.q.data_ptr(),
+                                              self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
+                                              self.pos.data_ptr(), dt, B, self.hq, self.hkv, D,
+                                              float(cfg["rope_theta"]), self.max_ctx, self._stream()),
+                           "rope_append")
+                _lib.check(lib.ng_attn_decode(self.q.data_ptr(), self.k_cache[li].data_ptr(),
+                                              self.v_cache[li].data_ptr(), self.ctx.data_ptr(),
+                                              self.attn.data_ptr(), dt, B, self.hq, self.hkv, D,
+                                              self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D),
+                                              self.attn_ws.data_ptr(), self.attn_ws.numel(),
+                                              self._stream()), "attn_decode")
             self._gemv(self.attn, w["o"], self.o)
             self._allreduce(self.o)
             self._norm(self.o, self.res, w["mlp_norm"], self.xn)

@@ -87,8 +87,9 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("batch", [1, 3])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_decoder_matches_fp32_restatement(batch, dtype):
-    m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4)
+@pytest.mark.parametrize("fused", [True, False])
+def test_decoder_matches_fp32_restatement(batch, dtype, fused):
+    m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4, fused_rope=fused)
     ref = RefModel(m)
     g = torch.Generator().manual_seed(batch)
     for step in range(6):
