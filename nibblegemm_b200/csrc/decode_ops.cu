@@ -258,46 +258,115 @@ __global__ void attn_rope_partial_kernel(const void* __restrict__ qkv, void* __r
     }
     __syncthreads();
   }
-  float mx = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  constexpr int kB = 8;
-  for (int tb = t0; tb < t1; tb += kB) {
-    float kv[kB][4], vv[kB][4], sc[kB];
+  // Warps take interleaved positions; each K / V row is loaded once and used
+  // for all G query heads of this KV head (q of every head held by each warp).
+  constexpr int kMaxG = 8;
+  float qa[kMaxG][4];
+#pragma unroll
+  for (int h = 0; h < kMaxG; ++h) {
+    if (h < G) {
+      if (h == warp) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qa[h][j] = qv[j];
+      }
+    }
+  }
+  // share the rotated, scaled q of every head through shared memory
+  __shared__ float qs[kMaxG][kAttnD];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qs[warp][lane * 4 + j] = qv[j];
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < kMaxG; ++h)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qa[h][j] = h < G ? qs[h][lane * 4 + j] : 0.f;
+  float mx[kMaxG], sum[kMaxG], acc[kMaxG][4];
+#pragma unroll
+  for (int h = 0; h < kMaxG; ++h) {
+    mx[h] = -INFINITY;
+    sum[h] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[h][j] = 0.f;
+  }
+  const int nw = blockDim.x >> 5;
+  constexpr int kB = 4;  // positions per warp loaded together
+  for (int tb = t0 + warp; tb < t1; tb += kB * nw) {
+    float kv[kB][4], vv[kB][4];
 #pragma unroll
     for (int u = 0; u < kB; ++u) {
-      if (tb + u < t1) {
-        const size_t kb = ((static_cast<size_t>(m) * max_ctx + tb + u) * Hkv + kh) * kAttnD + lane * 4;
+      const int t = tb + u * nw;
+      if (t < t1) {
+        const size_t kb = ((static_cast<size_t>(m) * max_ctx + t) * Hkv + kh) * kAttnD + lane * 4;
         ld_act4<BF16>(k_cache, kb, kv[u]);
         ld_act4<BF16>(v_cache, kb, vv[u]);
       }
     }
+    float sc[kB][kMaxG];
 #pragma unroll
-    for (int u = 0; u < kB; ++u) {
-      sc[u] = 0.f;
+    for (int u = 0; u < kB; ++u)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) sc[u] += qv[j] * kv[u][j];
-    }
+      for (int h = 0; h < kMaxG; ++h) {
+        sc[u][h] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[u][h] += qa[h][j] * kv[u][j];
+      }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int u = 0; u < kB; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+      for (int u = 0; u < kB; ++u)
+#pragma unroll
+        for (int h = 0; h < kMaxG; ++h)
+          if (h < G) sc[u][h] += __shfl_xor_sync(0xffffffffu, sc[u][h], o);
 #pragma unroll
     for (int u = 0; u < kB; ++u) {
-      if (tb + u >= t1) break;
-      const float nm = fmaxf(mx, sc[u]);
-      const float corr = __expf(mx - nm), pw = __expf(sc[u] - nm);
-      sum = sum * corr + pw;
+      if (tb + u * nw >= t1) break;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] = acc[j] * corr + pw * vv[u][j];
-      mx = nm;
+      for (int h = 0; h < kMaxG; ++h) {
+        if (h >= G) continue;
+        const float nm = fmaxf(mx[h], sc[u][h]);
+        const float corr = __expf(mx[h] - nm), pw = __expf(sc[u][h] - nm);
+        sum[h] = sum[h] * corr + pw;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[h][j] = acc[h][j] * corr + pw * vv[u][j];
+        mx[h] = nm;
+      }
     }
   }
-  float* o = part + ((static_cast<size_t>(m) * Hq + qh) * splits + sp) * (2 + kAttnD);
-  if (lane == 0) {
-    o[0] = mx;
-    o[1] = sum;
-  }
+  // merge the warps' states per head (fixed warp order) and write the partial
+  __shared__ float ms_[kMaxG][kMaxG][2];          // [warp][head][max, sum]
+  __shared__ float as_[kMaxG][kMaxG][kAttnD];     // [warp][head][dim]
 #pragma unroll
-  for (int j = 0; j < 4; ++j) o[2 + lane * 4 + j] = acc[j];
+  for (int h = 0; h < kMaxG; ++h) {
+    if (h >= G) continue;
+    if (lane == 0) {
+      ms_[warp][h][0] = mx[h];
+      ms_[warp][h][1] = sum[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) as_[warp][h][lane * 4 + j] = acc[h][j];
+  }
+  __syncthreads();
+  {
+    const int h = warp;  // warp h writes head h of this group
+    float M_ = -INFINITY;
+    for (int w2 = 0; w2 < nw; ++w2) M_ = fmaxf(M_, ms_[w2][h][0]);
+    float S = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w2 = 0; w2 < nw; ++w2) {
+      const float mw = ms_[w2][h][0];
+      if (mw == -INFINITY) continue;
+      const float f = __expf(mw - M_);
+      S += f * ms_[w2][h][1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) A[j] += f * as_[w2][h][lane * 4 + j];
+    }
+    float* o = part + ((static_cast<size_t>(m) * Hq + kh * G + h) * splits + sp) * (2 + kAttnD);
+    if (lane == 0) {
+      o[0] = M_;
+      o[1] = S;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[2 + lane * 4 + j] = A[j];
+  }
 }
 
 // Combine the splits of one (token, q head) in split order: out[M, Hq, D].
@@ -491,7 +560,7 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
                                    size_t workspace_bytes, void* stream) {
   if (!qkv || !k_cache || !v_cache || !pos || !out || !workspace) return NG_ERR_NULL_POINTER;
   if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
-  if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || Hq / Hkv > 32 || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || Hq / Hkv > 8 || max_ctx < 1) return NG_ERR_BAD_SHAPE;
   if (splits < 1 || splits > 256) return NG_ERR_BAD_ARGUMENT;
   if (workspace_bytes < ng_attn_workspace_bytes(M, Hq, splits)) return NG_ERR_BAD_ARGUMENT;
   auto st = static_cast<cudaStream_t>(stream);
