@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "ng_common.cuh"
 
@@ -208,14 +209,15 @@ __global__ void attn_partial_kernel(const void* __restrict__ q, const void* __re
 // lane l's dims 4l..4l+3 is lane l ^ 16); the CTA whose chunk holds the new
 // position rotates K, writes K and V there, and only then reads the chunk.
 // The context is pos[m] + 1 positions, clamped to the cache.
-template <bool BF16>
-__global__ void attn_rope_partial_kernel(const void* __restrict__ qkv, void* __restrict__ k_cache,
+template <bool BF16, int GQ>
+__global__ void __launch_bounds__(GQ * 32)
+    attn_rope_partial_kernel(const void* __restrict__ qkv, void* __restrict__ k_cache,
                                          void* __restrict__ v_cache, const int* __restrict__ pos,
                                          float* __restrict__ part, int Hq, int Hkv, int chunk,
                                          int splits, float scale, int max_ctx, float theta) {
   pdl_enter();
   const int kh = blockIdx.x, sp = blockIdx.y, m = blockIdx.z;
-  const int G = Hq / Hkv;
+  constexpr int G = GQ;  // query heads per KV head (compile time)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qh = kh * G + warp;
   const int p = pos[m];
@@ -260,17 +262,8 @@ __global__ void attn_rope_partial_kernel(const void* __restrict__ qkv, void* __r
   }
   // Warps take interleaved positions; each K / V row is loaded once and used
   // for all G query heads of this KV head (q of every head held by each warp).
-  constexpr int kMaxG = 8;
+  constexpr int kMaxG = GQ;
   float qa[kMaxG][4];
-#pragma unroll
-  for (int h = 0; h < kMaxG; ++h) {
-    if (h < G) {
-      if (h == warp) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) qa[h][j] = qv[j];
-      }
-    }
-  }
   // share the rotated, scaled q of every head through shared memory
   __shared__ float qs[kMaxG][kAttnD];
 #pragma unroll
@@ -560,7 +553,8 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
                                    size_t workspace_bytes, void* stream) {
   if (!qkv || !k_cache || !v_cache || !pos || !out || !workspace) return NG_ERR_NULL_POINTER;
   if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
-  if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || Hq / Hkv > 8 || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  if (Hq / Hkv != 1 && Hq / Hkv != 2 && Hq / Hkv != 4 && Hq / Hkv != 8) return NG_ERR_BAD_SHAPE;
   if (splits < 1 || splits > 256) return NG_ERR_BAD_ARGUMENT;
   if (workspace_bytes < ng_attn_workspace_bytes(M, Hq, splits)) return NG_ERR_BAD_ARGUMENT;
   auto st = static_cast<cudaStream_t>(stream);
@@ -568,14 +562,25 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
   const dim3 g1(Hkv, splits, M), g2(Hq, M);
   const int threads = (Hq / Hkv) * 32;
   auto* part = static_cast<float*>(workspace);
+  const int G = Hq / Hkv;
+  auto partial = [&](auto bf, auto gq) -> int {
+    constexpr bool B = decltype(bf)::value;
+    constexpr int GQ = decltype(gq)::value;
+    return launch_pdl(attn_rope_partial_kernel<B, GQ>, g1, dim3(GQ * 32), st, qkv, k_cache, v_cache,
+                      pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta);
+  };
+  auto by_g = [&](auto bf) -> int {
+    switch (G) {
+      case 1: return partial(bf, std::integral_constant<int, 1>{});
+      case 2: return partial(bf, std::integral_constant<int, 2>{});
+      case 4: return partial(bf, std::integral_constant<int, 4>{});
+      default: return partial(bf, std::integral_constant<int, 8>{});
+    }
+  };
   if (dtype == NG_DTYPE_BF16) {
-    if (int e = launch_pdl(attn_rope_partial_kernel<true>, g1, dim3(threads), st, qkv, k_cache, v_cache,
-                           pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta))
-      return e;
+    if (int e = by_g(std::true_type{})) return e;
     return launch_pdl(attn_combine_kernel<true>, g2, dim3(kAttnD), st, part, out, Hq, splits);
   }
-  if (int e = launch_pdl(attn_rope_partial_kernel<false>, g1, dim3(threads), st, qkv, k_cache, v_cache,
-                         pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta))
-    return e;
+  if (int e = by_g(std::false_type{})) return e;
   return launch_pdl(attn_combine_kernel<false>, g2, dim3(kAttnD), st, part, out, Hq, splits);
 }
