@@ -239,10 +239,7 @@ int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache, cons
 /* ng_rope_append + ng_attn_decode in one pass over the cache: q / K / V are
  * read from qkv [M, (Hq + 2 Hkv) * D], the new K / V row is written at pos[m]
  * (if inside the cache) by the chunk that reads it, and the context is
- * min(pos[m] + 1, max_ctx) rows.  One launch: the last chunk of each (token,
- * KV head) to finish combines the chunks.  The workspace
- * (ng_attn_workspace_bytes) must be zero before the first call (its arrival
- * counters; each call leaves them at zero); calls sharing it must not overlap. */
+ * min(pos[m] + 1, max_ctx) rows. */
 int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache, const int* pos, void* out,
                         int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,
                         float scale, float theta, void* workspace, size_t workspace_bytes,

@@ -214,8 +214,7 @@ __global__ void __launch_bounds__(GQ * 32)
     attn_rope_partial_kernel(const void* __restrict__ qkv, void* __restrict__ k_cache,
                                          void* __restrict__ v_cache, const int* __restrict__ pos,
                                          float* __restrict__ part, int Hq, int Hkv, int chunk,
-                                         int splits, float scale, int max_ctx, float theta,
-                                         void* __restrict__ out, unsigned int* __restrict__ counters) {
+                                         int splits, float scale, int max_ctx, float theta) {
   pdl_enter();
   const int kh = blockIdx.x, sp = blockIdx.y, m = blockIdx.z;
   constexpr int G = GQ;  // query heads per KV head (compile time)
@@ -361,35 +360,6 @@ __global__ void __launch_bounds__(GQ * 32)
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[2 + lane * 4 + j] = A[j];
   }
-  // The last split CTA of this (token, KV head) to finish merges every split in
-  // split order (deterministic), writes the heads' outputs and re-arms the counter.
-  __shared__ int last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0)
-    last = atomicAdd(&counters[m * Hkv + kh], 1u) == static_cast<unsigned int>(splits - 1);
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  {
-    const int h = warp;
-    const float* ph = part + (static_cast<size_t>(m) * Hq + kh * G + h) * splits * (2 + kAttnD);
-    float M_ = -INFINITY;
-    for (int s2 = 0; s2 < splits; ++s2) M_ = fmaxf(M_, __ldcg(ph + s2 * (2 + kAttnD)));
-    float S = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s2 = 0; s2 < splits; ++s2) {
-      const float ms = __ldcg(ph + s2 * (2 + kAttnD));
-      if (ms == -INFINITY) continue;
-      const float f = __expf(ms - M_);
-      S += f * __ldcg(ph + s2 * (2 + kAttnD) + 1);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) A[j] += f * __ldcg(ph + s2 * (2 + kAttnD) + 2 + lane * 4 + j);
-    }
-    const size_t ob = (static_cast<size_t>(m) * Hq + kh * G + h) * kAttnD + lane * 4;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) st_act<BF16>(out, ob + j, A[j] / S);
-  }
-  if (threadIdx.x == 0) counters[m * Hkv + kh] = 0u;
 }
 
 // Combine the splits of one (token, q head) in split order: out[M, Hq, D].
@@ -518,9 +488,7 @@ extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void*
 }
 
 extern "C" size_t ng_attn_workspace_bytes(int M, int Hq, int splits) {
-  // fp32 partials, then one arrival counter per (token, KV head) (<= M x Hq)
-  return static_cast<size_t>(M) * Hq * splits * (2 + kAttnD) * sizeof(float) +
-         static_cast<size_t>(M) * Hq * sizeof(unsigned int);
+  return static_cast<size_t>(M) * Hq * splits * (2 + kAttnD) * sizeof(float);
 }
 
 extern "C" int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache,
@@ -594,14 +562,12 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
   const dim3 g1(Hkv, splits, M), g2(Hq, M);
   const int threads = (Hq / Hkv) * 32;
   auto* part = static_cast<float*>(workspace);
-  auto* counters = reinterpret_cast<unsigned int*>(
-      static_cast<unsigned char*>(workspace) + static_cast<size_t>(M) * Hq * splits * (2 + kAttnD) * sizeof(float));
   const int G = Hq / Hkv;
   auto partial = [&](auto bf, auto gq) -> int {
     constexpr bool B = decltype(bf)::value;
     constexpr int GQ = decltype(gq)::value;
     return launch_pdl(attn_rope_partial_kernel<B, GQ>, g1, dim3(GQ * 32), st, qkv, k_cache, v_cache,
-                      pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta, out, counters);
+                      pos, part, Hq, Hkv, chunk, splits, scale, max_ctx, theta);
   };
   auto by_g = [&](auto bf) -> int {
     switch (G) {
@@ -611,7 +577,10 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
       default: return partial(bf, std::integral_constant<int, 8>{});
     }
   };
-  (void)g2;
-  (void)threads;
-  return dtype == NG_DTYPE_BF16 ? by_g(std::true_type{}) : by_g(std::false_type{});
+  if (dtype == NG_DTYPE_BF16) {
+    if (int e = by_g(std::true_type{})) return e;
+    return launch_pdl(attn_combine_kernel<true>, g2, dim3(kAttnD), st, part, out, Hq, splits);
+  }
+  if (int e = by_g(std::false_type{})) return e;
+  return launch_pdl(attn_combine_kernel<false>, g2, dim3(kAttnD), st, part, out, Hq, splits);
 }

@@ -128,8 +128,8 @@ class Llama3Decoder:
         self.best_scratch = torch.zeros(B, dtype=torch.int64, device=dev)  # argmax keys, re-armed per call
         self.best_val = torch.empty(B, dtype=torch.float32, device=dev)
         self.best_idx = torch.empty(B, dtype=torch.int64, device=dev)
-        self.attn_ws = torch.zeros(self.ext.lib.ng_attn_workspace_bytes(B, hq, attn_splits),
-                                   dtype=torch.uint8, device=dev)  # zero: attention arrival counters
+        self.attn_ws = torch.empty(self.ext.lib.ng_attn_workspace_bytes(B, hq, attn_splits),
+                                   dtype=torch.uint8, device=dev)
         self._peer = None
         if world > 1 and reduce == "peer":
             from .comm import PeerAllReduce
