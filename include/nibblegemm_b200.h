@@ -245,6 +245,17 @@ int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache, const int
                         float scale, float theta, void* workspace, size_t workspace_bytes,
                         void* stream);
 int ng_silu_mul(const void* gate_up, void* out, int dtype, int M, int I, void* stream);
+/* The cluster decode GEMV (algo 1 fp16 / 2 bf16) with the RMSNorm before it
+ * folded into its activation staging: h = x + residual_in, the GEMV input is
+ * h * rsqrt(mean(h^2) + eps) * norm_weight (rounded to the activation type, as
+ * ng_rmsnorm would store it), and h is written to residual_out (may be NULL;
+ * must not alias residual_in -- use two residual buffers alternately).
+ * M <= 16; [M, K] activations and residuals, norm_weight [K].  Saves the
+ * separate ng_rmsnorm launch before a projection. */
+int ng_gemv_w4a16_rmsnorm(const void* x, const void* residual_in, void* residual_out,
+                          const void* norm_weight, float eps, int x_dtype, const int32_t* qweight,
+                          const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                          void* stream);
 /* Row-wise argmax of logits [M, V] (ties: smallest index): value[m] (fp32) and
  * index[m] + index_offset (int64; the offset places a vocab shard).
  * best_scratch: M x 8 bytes, zero before the first call; each call leaves it

@@ -33,6 +33,7 @@ SIGNATURES = {
     "ng_attn_decode": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P,
                             ctypes.c_size_t, _P]),
     "ng_silu_mul": (_I, [_P, _P, _I, _I, _I, _P]),
+    "ng_gemv_w4a16_rmsnorm": (_I, [_P, _P, _P, _P, ctypes.c_float, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ng_attn_decode_rope": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float,
                                  ctypes.c_float, _P, ctypes.c_size_t, _P]),
     "ng_argmax": (_I, [_P, _I, _I, _I, ctypes.c_longlong, _P, _P, _P, _P]),

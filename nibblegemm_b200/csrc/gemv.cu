@@ -63,11 +63,56 @@ __device__ __forceinline__ void griddep_wait() {
 
 enum Path { kHalf2 = 0, kFloat2 = 1 };
 
+// Optional RMSNorm of the activations, folded into the staging of X (the
+// decode step's norm before the q|k|v and gate|up projections):
+//   h = x + res_in;  X = act(h * rsqrt(mean(h^2) + eps) * w);  res_out = h
+// with `act` the rounding to the activation type.  Every CTA re-reduces the
+// whole row (a few KB from L2); CTA (0, 0) writes res_out, which must not
+// alias res_in (the caller ping-pongs two residual buffers).  w == nullptr:
+// plain GEMV.
+struct NormArgs {
+  const unsigned short* res_in = nullptr;
+  unsigned short* res_out = nullptr;
+  const unsigned short* w = nullptr;
+  float eps = 0.f;
+};
+
+template <bool XBF16>
+__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (XBF16) {
+      f[2 * j] = __uint_as_float(w[j] << 16);
+      f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    } else {
+      const float2 t = __half22float2(h2_from_bits(w[j]));
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+}
+
+template <bool XBF16>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (XBF16) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&b);
+    } else {
+      w[j] = h2_bits(__floats2half2_rn(f[2 * j], f[2 * j + 1]));
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <int MT, bool XBF16, int PATH, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32)
     gemv_kernel(const void* __restrict__ x, const uint32_t* __restrict__ qw,
                 const __half* __restrict__ scales, void* __restrict__ y, int M, int K, int N,
-                int G, int rows_per_cta, int csize) {
+                int G, int rows_per_cta, int csize, NormArgs na) {
   extern __shared__ __align__(16) unsigned char smem[];
   using XS = typename std::conditional<PATH == kFloat2, float, __half>::type;
   XS* xs = reinterpret_cast<XS*>(smem);
@@ -203,12 +248,64 @@ __global__ void __launch_bounds__(WARPS * 32)
   int ch = warp;
   if (ch < nch) load_chunk(ch, qa, sa);  // weights only: no dependency on the previous kernel
   griddep_wait();                          // activations / outputs of the previous kernel
+  __shared__ float s_inv[MT];
+  if (na.w != nullptr) {  // ---- folded RMSNorm: per-token 1/rms over the whole row ----
+    __shared__ float s_red[WARPS][MT];
+    float ss[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) ss[m] = 0.f;
+    for (int c = tid; c < K / 8; c += WARPS * 32) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+          float a[8], b[8];
+          unpack8<XBF16>(ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(c) * 8), a);
+          unpack8<XBF16>(ld_ro_v4(na.res_in + static_cast<size_t>(m) * K + static_cast<size_t>(c) * 8), b);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss[m] += (a[j] + b[j]) * (a[j] + b[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      for (int o = 16; o > 0; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
+      if (lane == 0) s_red[warp][m] = ss[m];
+    }
+    __syncthreads();
+    if (tid < MT) {
+      float t = 0.f;
+      for (int w2 = 0; w2 < WARPS; ++w2) t += s_red[w2][tid];  // fixed order
+      s_inv[tid] = rsqrtf(t / static_cast<float>(K) + na.eps);
+    }
+    if (na.res_out != nullptr && blockIdx.x == 0 && blockIdx.y == 0) {
+      for (int i = tid; i < M * (K / 8); i += WARPS * 32) {
+        const int m = i / (K / 8), c = i - m * (K / 8);
+        float a[8], b[8];
+        unpack8<XBF16>(ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(c) * 8), a);
+        unpack8<XBF16>(ld_ro_v4(na.res_in + static_cast<size_t>(m) * K + static_cast<size_t>(c) * 8), b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] += b[j];
+        *reinterpret_cast<uint4*>(na.res_out + static_cast<size_t>(m) * K + static_cast<size_t>(c) * 8) =
+            pack8<XBF16>(a);
+      }
+    }
+    __syncthreads();
+  }
   // ---- stage X[:, kr0*8 : kr1*8) ------------------------------------------------
   for (int i = tid; i < MT * nrows; i += WARPS * 32) {
     const int m = i / nrows;
     const int r = i - m * nrows;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (m < M) v = ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(kr0 + r) * 8);
+    if (na.w != nullptr && m < M) {  // h = x + res_in, normalised, rounded to the activation type
+      float a[8], b[8], wf[8];
+      unpack8<XBF16>(v, a);
+      unpack8<XBF16>(ld_ro_v4(na.res_in + static_cast<size_t>(m) * K + static_cast<size_t>(kr0 + r) * 8), b);
+      unpack8<XBF16>(ld_ro_v4(na.w + static_cast<size_t>(kr0 + r) * 8), wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = (a[j] + b[j]) * s_inv[m] * wf[j];
+      v = pack8<XBF16>(a);
+    }
     XS* dst = xs + m * xstride + r * 8;
     if constexpr (PATH == kFloat2) {
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -302,7 +399,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 // ---------------------------------------------------------------------------
 template <int MT, bool XBF16, int PATH, int WARPS>
 int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N, int G,
-        int splits, const DeviceInfo& dev, cudaStream_t stream) {
+        int splits, const DeviceInfo& dev, cudaStream_t stream, NormArgs na = {}) {
   auto kern = gemv_kernel<MT, XBF16, PATH, WARPS>;
   constexpr int threads = WARPS * 32;
   constexpr int esz = PATH == kFloat2 ? 4 : 2;
@@ -363,17 +460,17 @@ int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return launch_status(cudaLaunchKernelEx(&cfg, kern, x, qw, s, y, M, K, N, G, rows_per_cta, C));
+  return launch_status(cudaLaunchKernelEx(&cfg, kern, x, qw, s, y, M, K, N, G, rows_per_cta, C, na));
 }
 
 template <bool XBF16, int PATH, int WARPS>
 int dispatch_m(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int K, int N,
-               int G, int splits, const DeviceInfo& dev, cudaStream_t st) {
-  if (M <= 1) return run<1, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  if (M <= 2) return run<2, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  if (M <= 4) return run<4, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  if (M <= 8) return run<8, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
-  return run<16, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st);
+               int G, int splits, const DeviceInfo& dev, cudaStream_t st, NormArgs na = {}) {
+  if (M <= 1) return run<1, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st, na);
+  if (M <= 2) return run<2, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st, na);
+  if (M <= 4) return run<4, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st, na);
+  if (M <= 8) return run<8, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st, na);
+  return run<16, XBF16, PATH, WARPS>(x, qw, s, y, M, K, N, G, splits, dev, st, na);
 }
 
 template <bool XBF16, int PATH>
@@ -453,4 +550,34 @@ extern "C" size_t ng_gemv_workspace_bytes(int M, int N) {
   ngb::DeviceInfo dev;
   if (M < 1 || M > 16 || N <= 0 || ngb::current_device_info(&dev) != NG_OK) return 0;
   return ngb::gemv_ring_workspace_bytes(N, dev);
+}
+
+extern "C" int ng_gemv_w4a16_rmsnorm(const void* x, const void* residual_in, void* residual_out,
+                                     const void* norm_weight, float eps, int x_dtype,
+                                     const int32_t* qweight, const uint16_t* scales, void* y, int M,
+                                     int K, int N, int group_size, void* stream) {
+  using namespace ngb;
+  if (!x || !residual_in || !norm_weight || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (residual_out == residual_in) return NG_ERR_BAD_ARGUMENT;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || K % 8 != 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (!aligned(x, 16) || !aligned(residual_in, 16) || !aligned(norm_weight, 16) ||
+      (residual_out && !aligned(residual_out, 16)) || !aligned(qweight, 16) || !aligned(scales, 8) ||
+      !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  NormArgs na;
+  na.res_in = static_cast<const unsigned short*>(residual_in);
+  na.res_out = static_cast<unsigned short*>(residual_out);
+  na.w = static_cast<const unsigned short*>(norm_weight);
+  na.eps = eps;
+  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NG_DTYPE_BF16)
+    return dispatch_m<true, kFloat2, 8>(x, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+  return dispatch_m<false, kHalf2, 8>(x, q, s, y, M, K, N, group_size, 0, dev, strm, na);
 }

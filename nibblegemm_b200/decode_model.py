@@ -58,11 +58,13 @@ class Llama3Decoder:
                  layers: Optional[int] = None, rank: int = 0, world: int = 1,
                  device: Optional[torch.device] = None, seed: int = 0,
                  dtype: torch.dtype = torch.float16, group_size: int = 128,
-                 reduce: str = "peer", attn_splits: int = 32, fused_rope: bool = True):
+                 reduce: str = "peer", attn_splits: int = 32, fused_rope: bool = True,
+                 fused_norm: bool = True):
         self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
         self.max_ctx, self.attn_splits, self.fused_rope = max_ctx, attn_splits, fused_rope
+        self.fused_norm = fused_norm
         H, D = cfg["hidden"], cfg["head_dim"]
         hq, hkv, inter = cfg["heads"] // world, cfg["kv_heads"] // world, cfg["intermediate"] // world
         if cfg["heads"] % world or cfg["kv_heads"] % world or cfg["intermediate"] % world:
@@ -116,6 +118,7 @@ class Llama3Decoder:
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.ctx = torch.ones(B, dtype=torch.int32, device=dev)
         self.res = torch.zeros(B, H, device=dev, dtype=dtype)
+        self.res2 = torch.zeros(B, H, device=dev, dtype=dtype)  # ping-pong partner (folded norms)
         self.xn = torch.empty(B, H, device=dev, dtype=dtype)
         self.qkv = torch.empty(B, (hq + 2 * hkv) * D, device=dev, dtype=dtype)
         self.q = torch.empty(B, hq * D, device=dev, dtype=dtype)
@@ -153,6 +156,13 @@ class Llama3Decoder:
         else:
             torch.distributed.all_reduce(t)
 
+    def _norm_gemv(self, x, res_in, res_out, norm_w, wq, out):
+        """RMSNorm folded into the projection's activation staging."""
+        _lib.check(self.ext.lib.ng_gemv_w4a16_rmsnorm(
+            x.data_ptr(), res_in.data_ptr(), res_out.data_ptr(), norm_w.data_ptr(), float(self.cfg["eps"]),
+            _DT[self.dtype], wq.qweight.data_ptr(), wq.scales.data_ptr(), out.data_ptr(), x.size(0),
+            wq.K, wq.N, wq.group_size, self._stream()), "gemv_w4a16_rmsnorm")
+
     def _norm(self, x, res, w, y):
         _lib.check(self.ext.lib.ng_rmsnorm(x.data_ptr(), res.data_ptr() if res is not None else None,
                                            w.data_ptr(), y.data_ptr(), _DT[self.dtype], x.size(0),
@@ -170,8 +180,11 @@ class Llama3Decoder:
         self.res.zero_()
         delta = x
         for li, w in enumerate(self.w):
-            self._norm(delta, self.res, w["attn_norm"], self.xn)
-            self._gemv(self.xn, w["qkv"], self.qkv)
+            if self.fused_norm:  # res -> res2 (h = delta + res), then res2 -> res below
+                self._norm_gemv(delta, self.res, self.res2, w["attn_norm"], w["qkv"], self.qkv)
+            else:
+                self._norm(delta, self.res, w["attn_norm"], self.xn)
+                self._gemv(self.xn, w["qkv"], self.qkv)
             if self.fused_rope:  # RoPE + KV append inside the attention kernel
                 _lib.check(lib.ng_attn_decode_rope(
                     self.qkv.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
@@ -192,8 +205,11 @@ class Llama3Decoder:
                                               self._stream()), "attn_decode")
             self._gemv(self.attn, w["o"], self.o)
             self._allreduce(self.o)
-            self._norm(self.o, self.res, w["mlp_norm"], self.xn)
-            self._gemv(self.xn, w["gu"], self.gu)
+            if self.fused_norm:
+                self._norm_gemv(self.o, self.res2, self.res, w["mlp_norm"], w["gu"], self.gu)
+            else:
+                self._norm(self.o, self.res, w["mlp_norm"], self.xn)
+                self._gemv(self.xn, w["gu"], self.gu)
             _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
                                        self._stream()), "silu_mul")
             self._gemv(self.act, w["down"], self.down)

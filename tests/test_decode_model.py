@@ -89,7 +89,8 @@ def _rel(a, b):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("fused", [True, False])
 def test_decoder_matches_fp32_restatement(batch, dtype, fused):
-    m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4, fused_rope=fused)
+    m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4, fused_rope=fused,
+                      fused_norm=fused)
     ref = RefModel(m)
     g = torch.Generator().manual_seed(batch)
     for step in range(6):
@@ -193,3 +194,31 @@ def test_argmax_kernel_matches_torch_and_rearms(dtype, M, V):
         ref_v, ref_i = x.float().max(dim=1)  # torch returns the first maximal index
         assert torch.equal(idx - 100, ref_i) and torch.equal(val, ref_v)
         assert int(scratch.count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 6144), (3, 512, 1028), (16, 1024, 256)])
+def test_rmsnorm_folded_gemv_matches_separate_kernels(dtype, M, K, N):
+    """ng_gemv_w4a16_rmsnorm == ng_rmsnorm then the cluster GEMV (same rounding
+    of the normalised activations), and the new residual equals x + residual."""
+    ext, lib = ng.extension(), ng.extension().lib
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    x = torch.randn(M, K, generator=g, device="cuda").to(dtype)
+    res = torch.randn(M, K, generator=g, device="cuda").to(dtype)
+    nw = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).to(dtype)
+    qw = ng.quantize(torch.randn(K, N) * 0.02).to("cuda")
+    code = 1 if dtype == torch.bfloat16 else 0
+    st = torch.cuda.current_stream().cuda_stream
+    y = torch.empty(M, N, dtype=dtype, device="cuda")
+    res_out = torch.empty_like(res)
+    assert lib.ng_gemv_w4a16_rmsnorm(x.data_ptr(), res.data_ptr(), res_out.data_ptr(), nw.data_ptr(), 1e-5,
+                                     code, qw.qweight.data_ptr(), qw.scales.data_ptr(), y.data_ptr(),
+                                     M, K, N, 128, st) == 0
+    r2, xn = res.clone(), torch.empty_like(x)
+    assert lib.ng_rmsnorm(x.data_ptr(), r2.data_ptr(), nw.data_ptr(), xn.data_ptr(), code, M, K, 1e-5, st) == 0
+    ref = ext.gemv_w4a16(xn, qw.qweight, qw.scales, 128, algo=2 if code else 1)
+    torch.cuda.synchronize()
+    assert torch.equal(res_out, r2)
+    d = (y.float() - ref.float()).abs().max().item() / ref.float().abs().max().item()
+    assert d < (1e-2 if code else 2e-3), d
+    assert ext.device_status() == 0
