@@ -6,10 +6,14 @@ the same Python names, the same ``QuantLinear`` -- with hand-written sm_100a
 kernels behind a C ABI (``include/nibblegemm_b200.h``).
 """
 from .ops import DECODE_MAX_M, QuantLinear, dequant, extension, gemm, gemv, matmul
+from .decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL, Llama3Decoder
 from .importers import from_autogptq, to_autogptq
 from .quant import QuantizedWeight, pack_nibbles, quantize, unpack_nibbles
 
 __all__ = [
+    "LLAMA3_8B_MODEL",
+    "LLAMA3_70B_MODEL",
+    "Llama3Decoder",
     "from_autogptq",
     "to_autogptq",
     "DECODE_MAX_M",

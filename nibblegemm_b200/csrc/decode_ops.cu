@@ -560,7 +560,6 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
   auto st = static_cast<cudaStream_t>(stream);
   const int chunk = (max_ctx + splits - 1) / splits;
   const dim3 g1(Hkv, splits, M), g2(Hq, M);
-  const int threads = (Hq / Hkv) * 32;
   auto* part = static_cast<float*>(workspace);
   const int G = Hq / Hkv;
   auto partial = [&](auto bf, auto gq) -> int {
