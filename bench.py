@@ -50,6 +50,7 @@ WORKLOADS = {
     "gemm": dict(M=2048, K=4096, N=14336, G=128, name="W4A16 prefill GEMM M=2048 K=4096 N=14336 g128 fp16 (BASELINE config 3)"),
     "step8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 projection stack (224 projections), batch 1, tensor-parallel over the ranks"),
     "decode8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 full decode step (BASELINE config 4): attention over a 1024-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch 1, tensor-parallel over the ranks"),
+    "decode70b": dict(M=1, K=8192, N=28672, G=128, name="Llama-3-70B INT4 g128 full decode step (BASELINE config 5): attention over a 2048-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch --batch, tensor-parallel over the ranks"),
     "sweep2": dict(M=1, K=4096, N=14336, G=128, name="BASELINE config 2: decode GEMV sweep M x (K, N), eager and graph, vs cuBLAS fp16"),
     "sweep3": dict(M=2048, K=4096, N=14336, G=128, name="BASELINE config 3: prefill GEMM sweep M x (K, N) x {fp16, bf16}"),
 }
@@ -287,7 +288,9 @@ def run_reference(args, rank):
 
 
 def run_decode(args, wl, world, rank, local, dist):
-    """Tokens/s of the full Llama-3-8B decode step.
+    """Tokens/s of the full Llama-3-8B decode step (with
+    ``--workload decode70b`` the Llama-3-70B step of config 5: context 2048,
+    ``--batch`` sequences).
 
     One step = one token through embedding, 32 layers (RMSNorm, fused q|k|v
     GEMV, GQA attention with RoPE + KV append over 1024 cached positions, o GEMV,
@@ -295,10 +298,13 @@ def run_decode(args, wl, world, rank, local, dist):
     final norm, fp16 lm_head and argmax; captured once in a CUDA graph and
     replayed with the position held at 1023 (context 1024).  Strong scaling.
     """
-    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, Llama3Decoder
-    cfg = LLAMA3_8B_MODEL
-    m = Llama3Decoder(cfg, batch=1, max_ctx=1024, rank=rank, world=world, reduce=args.reduce)
-    m.pos.fill_(1023)
+    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL, Llama3Decoder
+    big = args.workload == "decode70b"
+    cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
+    ctx = 2048 if big else 1024
+    batch = args.batch if big else 1
+    m = Llama3Decoder(cfg, batch=batch, max_ctx=ctx, rank=rank, world=world, reduce=args.reduce)
+    m.pos.fill_(ctx - 1)
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
@@ -333,8 +339,8 @@ def run_decode(args, wl, world, rank, local, dist):
         ms = t.item()
     per_ms = ms / args.steps
     # e2e: the token id in from pinned host memory, the step (graph), the next id back
-    tok_host = torch.zeros(1, dtype=torch.int64).pin_memory()
-    out_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+    tok_host = torch.zeros(batch, dtype=torch.int64).pin_memory()
+    out_host = torch.zeros(batch, dtype=torch.int64).pin_memory()
     e2e_steps = max(3, min(args.steps, 50))
     if dist:
         dist.barrier()
@@ -355,28 +361,29 @@ def run_decode(args, wl, world, rank, local, dist):
         e2e_ms = t.item()
     if rank == 0:
         hbm, _, src = measured_peaks()
-        kv = 2 * cfg["layers"] * 1024 * m.hkv * cfg["head_dim"] * 2
-        nbytes = m.weight_bytes + m.lm_head.numel() * 2 + kv + cfg["hidden"] * 2
+        kv = 2 * cfg["layers"] * ctx * m.hkv * cfg["head_dim"] * 2 * batch
+        nbytes = m.weight_bytes + m.lm_head.numel() * 2 + kv + cfg["hidden"] * 2 * batch
         achieved = nbytes / (per_ms * 1e-3) / 1e9
         # ours per layer: 4 GEMVs (2 with the RMSNorm folded in), 2 attention (RoPE + KV
         # append folded in), SwiGLU (+2 peer all-reduces); then the final norm and 2 argmax
-        launches = 32 * 7 + 3 + (64 if (world > 1 and args.reduce == "peer") else 0)
+        L = cfg["layers"]
+        launches = L * 7 + 3 + (2 * L if (world > 1 and args.reduce == "peer") else 0)
         line = {
-            "metric": METRIC, "value": round(1000.0 / per_ms, 2), "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC, "value": round(1000.0 * batch / per_ms, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic random-init Llama-3-8B (seeded N(0,0.02) weights, RTN INT4 g128), batch 1",
-            "config": {"workload": wl["name"], "layers": 32, "hidden": 4096, "heads": 32, "kv_heads": 8,
-                       "intermediate": 14336, "vocab": 128256, "context": 1024, "group_size": 128,
-                       "batch": 1, "parallelism": f"tp{world}",
+            "data": f"synthetic random-init {'Llama-3-70B' if big else 'Llama-3-8B'} (seeded N(0,0.02) weights, RTN INT4 g128), batch {batch}",
+            "config": {"workload": wl["name"], "layers": L, "hidden": cfg["hidden"], "heads": cfg["heads"],
+                       "kv_heads": cfg["kv_heads"], "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
+                       "context": ctx, "group_size": 128, "batch": batch, "parallelism": f"tp{world}",
                        "tp_reduce": (args.reduce if world > 1 else None),
-                       "l2": "4.8 GB read per token (>> L2)",
-                       "timing": "one CUDA graph per token, replayed `steps` times"},
+                       "l2": f"{nbytes / 1e9:.1f} GB read per step (>> L2)",
+                       "timing": "one CUDA graph per step (every sequence advances one token), replayed `steps` times"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": None,
                          "peak_source": f"{src} copy bandwidth", "algorithmic_bytes_per_step_per_rank": nbytes},
-            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 8, "path": "token id in -> Llama3Decoder.step() graph -> next id out"},
+            "e2e": {"value": round(1000.0 * batch / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * batch,
+                    "d2h_bytes_per_step": 8 * batch, "path": "token ids in -> Llama3Decoder.step() graph -> next ids out"},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
@@ -488,6 +495,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
                     help="tensor-parallel all-reduce of the step8b workload")
+    ap.add_argument("--batch", type=int, default=1, help="sequences per step (decode70b)")
     ap.add_argument("--algo", type=int, default=0, help="GEMV schedule (see ng_gemv_w4a16)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: run the op warmup+1 times eagerly on one GPU and exit")
@@ -512,7 +520,7 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.workload == "step8b":
         return run_step(args, wl, world, rank, local, dist)
-    if args.workload == "decode8b":
+    if args.workload in ("decode8b", "decode70b"):
         return run_decode(args, wl, world, rank, local, dist)
     if args.workload in ("sweep2", "sweep3"):
         if rank == 0:
