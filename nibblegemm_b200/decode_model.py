@@ -64,7 +64,9 @@ class Llama3Decoder:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
         self.max_ctx, self.attn_splits, self.fused_rope = max_ctx, attn_splits, fused_rope
-        self.fused_norm = fused_norm
+        # The folded norm re-reduces each token's row in every CTA: worth it for a
+        # few tokens only (measured: a loss at batch 16).
+        self.fused_norm = fused_norm and batch <= 4
         H, D = cfg["hidden"], cfg["head_dim"]
         hq, hkv, inter = cfg["heads"] // world, cfg["kv_heads"] // world, cfg["intermediate"] // world
         if cfg["heads"] % world or cfg["kv_heads"] % world or cfg["intermediate"] % world:
@@ -144,9 +146,10 @@ class Llama3Decoder:
         return torch.cuda.current_stream().cuda_stream
 
     def _gemv(self, x, w, out):
-        # cluster GEMV (algo 1 / 2): fastest in a mixed chain of shapes
-        self.ext.gemv_w4a16(x, w.qweight, w.scales, w.group_size,
-                            algo=2 if x.dtype == torch.bfloat16 else 1, out=out)
+        # batch <= 4: the cluster GEMV (algo 1 / 2), fastest in this mixed chain of
+        # shapes; larger batches: the library's default routing (tensor-pipe ring)
+        algo = (2 if x.dtype == torch.bfloat16 else 1) if x.size(0) <= 4 else 0
+        self.ext.gemv_w4a16(x, w.qweight, w.scales, w.group_size, algo=algo, out=out)
 
     def _allreduce(self, t):
         if self.world == 1:
