@@ -52,6 +52,7 @@ WORKLOADS = {
     "decode8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 full decode step (BASELINE config 4): attention over a 1024-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch 1, tensor-parallel over the ranks"),
     "decode70b": dict(M=1, K=8192, N=28672, G=128, name="Llama-3-70B INT4 g128 full decode step (BASELINE config 5): attention over a 2048-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch --batch, tensor-parallel over the ranks"),
     "sweep2": dict(M=1, K=4096, N=14336, G=128, name="BASELINE config 2: decode GEMV sweep M x (K, N), eager and graph, vs cuBLAS fp16"),
+    "readfloor": dict(M=1, K=4096, N=14336, G=128, name="transfer-size floor: config-1 GEMV at N x 1/2/4/8 beside a torch fp32 sum reading the same bytes"),
     "sweep3": dict(M=2048, K=4096, N=14336, G=128, name="BASELINE config 3: prefill GEMM sweep M x (K, N) x {fp16, bf16}"),
 }
 
@@ -94,6 +95,41 @@ def _eager_us(fn, n):
     b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) * 1e3 / n
+
+
+def run_readfloor(args, local):
+    """How fast can one launch read B bytes?  For the config-1 byte count and
+    2x/4x/8x it, our M=1 GEMV (K=4096, N scaled) and a torch ``sum`` (fp32
+    accumulate) over a buffer of the same algorithmic bytes, both replayed from a
+    CUDA graph with operands rotated over more than L2.  One JSON line per size."""
+    import nibblegemm_b200 as ng
+    from oracle import quant_oracle as qo  # seeded synthetic inputs (generator only)
+    ext = ng.extension()
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    hbm, _, src = measured_peaks()
+    stream = torch.cuda.Stream()
+    K, G = 4096, 128
+    for r in (1, 2, 4, 8):
+        N = 14336 * r
+        x, q, sc = qo.synthetic_case(1, K, N, group_size=G, seed=3)
+        nb = algo_bytes(1, K, N, G)
+        nrot = max(2, -(-3 * l2 // nb))
+        Q = [torch.from_numpy(q).cuda() for _ in range(nrot)]
+        S = [torch.from_numpy(sc).cuda() for _ in range(nrot)]
+        X = torch.from_numpy(x).cuda()
+        Y = torch.empty(1, N, dtype=torch.float16, device="cuda")
+        ours = lambda i: ext.gemv_w4a16(X, Q[i % nrot], S[i % nrot], G, out=Y)
+        B = [torch.randn(nb // 2, device="cuda").half() for _ in range(nrot)]
+        out = torch.empty((), dtype=torch.float32, device="cuda")
+        red = lambda i: out.copy_(torch.sum(B[i % nrot], dtype=torch.float32))
+        ug, ur = _graph_us(ours, 100, stream), _graph_us(red, 100, stream)
+        print(json.dumps({
+            "readfloor": "config1", "bytes": nb, "N": N, "gemv_us": round(ug, 2),
+            "gemv_GBs": round(nb / ug / 1e3, 1), "torch_sum_us": round(ur, 2),
+            "torch_sum_GBs": round(nb / ur / 1e3, 1), "gemv_frac_hbm": round(nb / ug / 1e3 / hbm, 3),
+            "torch_sum_frac_hbm": round(nb / ur / 1e3 / hbm, 3), "peak_source": src}), flush=True)
+        del Q, S, B
+        torch.cuda.empty_cache()
 
 
 def run_sweep(args, local):
@@ -522,6 +558,10 @@ def main():
         return run_step(args, wl, world, rank, local, dist)
     if args.workload in ("decode8b", "decode70b"):
         return run_decode(args, wl, world, rank, local, dist)
+    if args.workload == "readfloor":
+        if rank == 0:
+            run_readfloor(args, local)
+        return
     if args.workload in ("sweep2", "sweep3"):
         if rank == 0:
             run_sweep(args, local)

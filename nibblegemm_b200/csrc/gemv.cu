@@ -517,20 +517,27 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
     }
   }
   // Default schedule (measured on B200, M <= 8, no cluster-kernel options):
-  //   * >= 96 column tiles (N >= 12288), M <= 8 and M >= 2 or K <= 4096: the ring
-  //     with one CTA per tile (its CTAs sweep the rows in lockstep);
+  //   * 96 column tiles (N >= 12288) up to one per SM, M <= 8 and M >= 2 or
+  //     K <= 4096: the ring with one CTA per tile (its CTAs sweep the rows in
+  //     lockstep);
+  //   * more column tiles than SMs, M <= 8: the ring with its own K split;
   //   * M = 3..4 and a packed weight >= 12 MiB: the stream-K ring (all SMs);
   //   * M > 4 (up to 16): the ring with its own K split;
   //   * otherwise the cluster kernel.
   if (algo == 0 && block_threads == 0 && splits <= 8) {
     const int tiles = (N + 127) / 128;
     const double wbytes = static_cast<double>(K) * N / 2.0;
-    if (tiles >= 96 && M <= 8 && (M > 1 || K <= 4096)) {
+    if (tiles >= 96 && tiles <= dev.sm_count && M <= 8 && (M > 1 || K <= 4096)) {
       // One K slice per tile: the grid leaves SMs free, where the next kernel's
       // CTAs start streaming early (measured: faster in a chain than the
       // all-SM head/tail plan, 9.3 vs 16.2 us at config 1).
       algo = 5;
       if (splits == 0) splits = 1;
+    } else if (tiles > dev.sm_count && M <= 8) {
+      // More tiles than SMs: one slice per tile runs in two unbalanced waves
+      // (measured K=4096 N=57344 M=1: 55.8 us vs 29.5 us with the ring's own
+      // K split; M=8 is equal either way).
+      algo = 5;
     } else if (M > 4 || (M >= 3 && wbytes >= 12.0 * (1 << 20))) {  // includes M = 9..16
       algo = 5;
     }

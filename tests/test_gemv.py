@@ -275,3 +275,14 @@ def test_ring_tensor_pipe_two_token_tiles(M, K, N, act):
     check(ng.gemv(X, qw, algo=5), ref, X.dtype)
     check(ng.gemv(X, qw), ref, X.dtype)
     assert ng.extension().device_status() == 0
+
+
+# More column tiles than SMs (the Llama gate|up and 70B widths): the default
+# routing takes the ring with its own K split there, not one slice per tile.
+@pytest.mark.parametrize("K,N", [(4096, 28672), (8192, 28672), (4096, 57344)])
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_wide_shapes_default_routing(K, N, M):
+    X, qw, ref = make_case(M, K, N, 128, seed=K + N + 3 * M)
+    y = ng.gemv(X, qw)
+    check(y, ref, torch.float16)
+    assert torch.equal(y, ng.gemv(X, qw, algo=5))
