@@ -49,7 +49,7 @@ WORKLOADS = {
     "gemv": dict(M=1, K=4096, N=14336, G=128, name="W4A16 decode GEMV M=1 K=4096 N=14336 g128 fp16 (BASELINE config 1)"),
     "gemm": dict(M=2048, K=4096, N=14336, G=128, name="W4A16 prefill GEMM M=2048 K=4096 N=14336 g128 fp16 (BASELINE config 3)"),
     "step8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 projection stack (224 projections), batch 1, tensor-parallel over the ranks"),
-    "decode8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 full decode step (BASELINE config 4): attention over a 1024-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch 1, tensor-parallel over the ranks"),
+    "decode8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 full decode step (BASELINE config 4): attention over a 1024-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch --batch (default 1), tensor-parallel over the ranks"),
     "decode70b": dict(M=1, K=8192, N=28672, G=128, name="Llama-3-70B INT4 g128 full decode step (BASELINE config 5): attention over a 2048-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch --batch, tensor-parallel over the ranks"),
     "sweep2": dict(M=1, K=4096, N=14336, G=128, name="BASELINE config 2: decode GEMV sweep M x (K, N), eager and graph, vs cuBLAS fp16"),
     "readfloor": dict(M=1, K=4096, N=14336, G=128, name="transfer-size floor: config-1 GEMV at N x 1/2/4/8 beside a torch fp32 sum reading the same bytes"),
@@ -338,8 +338,9 @@ def run_decode(args, wl, world, rank, local, dist):
     big = args.workload == "decode70b"
     cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
     ctx = 2048 if big else 1024
-    batch = args.batch if big else 1
-    m = Llama3Decoder(cfg, batch=batch, max_ctx=ctx, rank=rank, world=world, reduce=args.reduce)
+    batch = args.batch
+    m = Llama3Decoder(cfg, batch=batch, max_ctx=ctx, rank=rank, world=world, reduce=args.reduce,
+                      wide_split=not args.no_wide_split)
     m.pos.fill_(ctx - 1)
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
@@ -531,7 +532,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
                     help="tensor-parallel all-reduce of the step8b workload")
-    ap.add_argument("--batch", type=int, default=1, help="sequences per step (decode70b)")
+    ap.add_argument("--batch", type=int, default=1, help="sequences per step (decode8b, decode70b)")
+    ap.add_argument("--no-wide-split", action="store_true",
+                    help="decode workloads: keep wide projections on the cluster GEMV")
     ap.add_argument("--algo", type=int, default=0, help="GEMV schedule (see ng_gemv_w4a16)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling target: run the op warmup+1 times eagerly on one GPU and exit")

@@ -59,7 +59,7 @@ class Llama3Decoder:
                  device: Optional[torch.device] = None, seed: int = 0,
                  dtype: torch.dtype = torch.float16, group_size: int = 128,
                  reduce: str = "peer", attn_splits: int = 32, fused_rope: bool = True,
-                 fused_norm: bool = True):
+                 fused_norm: bool = True, wide_split: bool = True):
         self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
@@ -67,6 +67,13 @@ class Llama3Decoder:
         # The folded norm re-reduces each token's row in every CTA: worth it for a
         # few tokens only (measured: a loss at batch 16).
         self.fused_norm = fused_norm and batch <= 4
+        # Projections with more 128-column tiles than SMs (gate|up) run faster on
+        # the library's split ring than on the cluster kernel the batch <= 4
+        # chain uses elsewhere, so they keep their norm separate.  Measured in
+        # the full 8B step: 1029 -> 1220 tok/s at batch 4, but 464 -> 405 at
+        # batch 1, where the cluster kernel's free SMs let the next kernel start.
+        self.wide_split = wide_split and batch >= 2
+        self._sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         H, D = cfg["hidden"], cfg["head_dim"]
         hq, hkv, inter = cfg["heads"] // world, cfg["kv_heads"] // world, cfg["intermediate"] // world
         if cfg["heads"] % world or cfg["kv_heads"] % world or cfg["intermediate"] % world:
@@ -145,10 +152,14 @@ class Llama3Decoder:
     def _stream(self):
         return torch.cuda.current_stream().cuda_stream
 
+    def _wide(self, w):
+        return self.wide_split and (w.N + 127) // 128 > self._sms
+
     def _gemv(self, x, w, out):
         # batch <= 4: the cluster GEMV (algo 1 / 2), fastest in this mixed chain of
-        # shapes; larger batches: the library's default routing (tensor-pipe ring)
-        algo = (2 if x.dtype == torch.bfloat16 else 1) if x.size(0) <= 4 else 0
+        # shapes; larger batches and wide projections: the library's default
+        # routing (tensor-pipe ring)
+        algo = (2 if x.dtype == torch.bfloat16 else 1) if x.size(0) <= 4 and not self._wide(w) else 0
         self.ext.gemv_w4a16(x, w.qweight, w.scales, w.group_size, algo=algo, out=out)
 
     def _allreduce(self, t):
@@ -182,12 +193,22 @@ class Llama3Decoder:
         x = torch.nn.functional.embedding(self.tokens, self.embed)
         self.res.zero_()
         delta = x
-        for li, w in enumerate(self.w):
-            if self.fused_norm:  # res -> res2 (h = delta + res), then res2 -> res below
-                self._norm_gemv(delta, self.res, self.res2, w["attn_norm"], w["qkv"], self.qkv)
+        # The residual stream lives in `res`; a folded norm writes h to the other
+        # buffer of the pair and the stream moves there (fixed per model, so a
+        # captured graph replays the same buffers).
+        res, spare = self.res, self.res2
+
+        def norm_proj(x_in, norm_w, wq, out):
+            nonlocal res, spare
+            if self.fused_norm and not self._wide(wq):
+                self._norm_gemv(x_in, res, spare, norm_w, wq, out)
+                res, spare = spare, res
             else:
-                self._norm(delta, self.res, w["attn_norm"], self.xn)
-                self._gemv(self.xn, w["qkv"], self.qkv)
+                self._norm(x_in, res, norm_w, self.xn)
+                self._gemv(self.xn, wq, out)
+
+        for li, w in enumerate(self.w):
+            norm_proj(delta, w["attn_norm"], w["qkv"], self.qkv)
             if self.fused_rope:  # RoPE + KV append inside the attention kernel
                 _lib.check(lib.ng_attn_decode_rope(
                     self.qkv.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
@@ -208,17 +229,13 @@ class Llama3Decoder:
                                               self._stream()), "attn_decode")
             self._gemv(self.attn, w["o"], self.o)
             self._allreduce(self.o)
-            if self.fused_norm:
-                self._norm_gemv(self.o, self.res2, self.res, w["mlp_norm"], w["gu"], self.gu)
-            else:
-                self._norm(self.o, self.res, w["mlp_norm"], self.xn)
-                self._gemv(self.xn, w["gu"], self.gu)
+            norm_proj(self.o, w["mlp_norm"], w["gu"], self.gu)
             _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
                                        self._stream()), "silu_mul")
             self._gemv(self.act, w["down"], self.down)
             self._allreduce(self.down)
             delta = self.down
-        self._norm(delta, self.res, self.final_norm, self.xn)
+        self._norm(delta, res, self.final_norm, self.xn)
         torch.mm(self.xn, self.lm_head.t(), out=self.logits)
         idx_out = self.tokens if self.world == 1 else self.best_idx
         _lib.check(self.ext.lib.ng_argmax(self.logits.data_ptr(), _DT[self.dtype], B, self.v1 - self.v0,

@@ -87,10 +87,15 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("batch", [1, 3])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("fused", [True, False])
-def test_decoder_matches_fp32_restatement(batch, dtype, fused):
+@pytest.mark.parametrize("fused,sms", [(True, None), (False, None), (True, 14), (True, 1)])
+def test_decoder_matches_fp32_restatement(batch, dtype, fused, sms):
     m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4, fused_rope=fused,
                       fused_norm=fused)
+    if sms is not None:
+        # pretend a smaller GPU: 14 SMs makes only gate|up (16 column tiles)
+        # "wide" (separate norm + split ring, the residual stream changes buffer
+        # once per layer), 1 SM makes every projection wide
+        m._sms = sms
     ref = RefModel(m)
     g = torch.Generator().manual_seed(batch)
     for step in range(6):
