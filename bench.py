@@ -1,13 +1,18 @@
 """Benchmark of the W4A16 hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemv|gemm]
+                    [--workload gemv|gemm|step8b|decode8b|decode70b|readfloor|sweep2|sweep3]
+                    [--batch B] [--reduce peer|nccl] [--algo A] [--no-wide-split]
 
 Workload (default ``gemv``): BASELINE config 1 -- the decode GEMV
 Y[1, 14336] = X[1, 4096] @ W4(4096 x 14336), group 128, fp16 activations, the
 shape the headline "decode GEMV us & HBM GB/s at M=1" is quoted on.  A step is
 one fused dequant-GEMV over one batch.  ``--workload gemm`` times BASELINE
-config 3's M=2048, K=4096, N=14336 prefill GEMM instead (TFLOP/s).
+config 3's M=2048, K=4096, N=14336 prefill GEMM instead (TFLOP/s).  The
+decode workloads (``step8b`` projection stack, ``decode8b`` / ``decode70b``
+full Llama-3 steps, tokens/s) replay one CUDA graph per token, tensor-parallel
+over torchrun ranks; ``readfloor``, ``sweep2`` and ``sweep3`` print one line
+per measured point (diagnostics, not the headline).
 
 * ``value``: algorithmic bytes (``K*N/2 + K/G*N*2 + M*K*2 + M*N*2``, the
   reference's byte model, bench/harness.py:243-255) per step x steps x ranks,
