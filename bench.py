@@ -282,9 +282,61 @@ def cpu_reference_sample(wl, seconds: float = 12.0, threads: int = 0):
             torch.get_num_threads())
 
 
+def run_reference_decode(args):
+    """Reference arm of the decode workloads: the reference's CPU path for one
+    token's projections (its model benchmark is the 7 projections of every
+    layer, bench/bench_model.py:43-125), each shape timed once per step with
+    ``reference_matmul`` (numpy dequantise + torch fp32 matmul) and scaled by the
+    layer count.  Attention, norms and the lm_head are not counted, which
+    favours the reference."""
+    from nibblegemm_b200.decode_step import LLAMA3_70B, LLAMA3_8B, layer_projections
+    from oracle import quant_oracle as qo
+    wl = WORKLOADS[args.workload]
+    cfg = LLAMA3_70B if args.workload == "decode70b" else LLAMA3_8B
+    batch = args.batch if args.workload != "step8b" else 1
+    cases = []
+    for i, (_, K, N, _) in enumerate(layer_projections(cfg)):
+        x, q, s = qo.synthetic_case(batch, K, N, group_size=128, seed=i)
+        cases.append((torch.from_numpy(x.astype(np.float32)), q, s, K))
+
+    def step():
+        t = 0.0
+        for xt, q, s, K in cases:
+            t0 = time.perf_counter()
+            W = qo.dequantize_np(q, s, 128, K).astype(np.float32)
+            (xt @ torch.from_numpy(W)).to(torch.float16)
+            t += time.perf_counter() - t0
+        return t * cfg["layers"]
+
+    for _ in range(3):  # warm-up passes (each pass is seconds)
+        step()
+    t0, times = time.perf_counter(), []
+    while len(times) < args.steps:
+        times.append(step())
+        if time.perf_counter() - t0 > 90.0:
+            break
+    per = sum(times) / len(times)
+    value = batch / per
+    sample = (f"{len(times)} passes over the 7 projection shapes of one {args.workload} layer at "
+              f"M={batch} (reference_matmul each), x {cfg['layers']} layers; projections only")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": 3, "ms_per_step": round(per * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (BASELINE distributions, seeded)",
+        "config": {"workload": wl["name"], "batch": batch, "group_size": 128},
+        "cpu_baseline": {"value": round(value, 6), "unit": "tok/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
+    if args.workload in ("step8b", "decode8b", "decode70b"):
+        return run_reference_decode(args)
     wl = WORKLOADS[args.workload]
     M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
     from oracle import quant_oracle as qo

@@ -40,3 +40,15 @@ def test_reference_arm_prints_one_contract_line():
 
 def test_reference_arm_other_ranks_print_nothing():
     assert _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
+
+
+def test_reference_arm_decode_workload_reports_tokens_per_second():
+    env = dict(os.environ)
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "step8b",
+                          "--steps", "1", "--warmup", "3"], cwd=ROOT, env=env,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    assert d["impl"] == "reference" and d["unit"] == "tok/s" and d["value"] > 0
+    assert d["warmup"] >= 3 and d["cpu_baseline"]["unit"] == "tok/s"
+    assert d["e2e"]["h2d_bytes_per_step"] == 0
