@@ -99,7 +99,7 @@ struct RingLayout {
 constexpr int kBoxRows = 8;  // packed rows per TMA box: 128 x 8 words = 4 KB
 
 // 2-D tiled TMA load of one (128-column, 8-row) box of the packed weight,
-// L2 evict-first (each weight byte is read once).  No multicast.
+// L2 evict-first (each weight byte is read once).
 __device__ __forceinline__ void tma_box_g2s(void* dst, const CUtensorMap* map, uint64_t* bar, int col,
                                             int row, uint64_t policy) {
   asm volatile(

@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100 asynchronous primitives used by the GEMM:
-// mbarriers, TMA tiled loads (no multicast), tensor-memory allocation,
+// mbarriers, TMA tiled loads into this CTA's shared memory, tensor-memory allocation,
 // tcgen05.mma / commit / ld, and the bounded wait every pipeline wait uses.
 #pragma once
 
@@ -74,7 +74,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ---------------------------------------------------------------------------
 // TMA: 2-D tiled load global -> shared, completion counted on an mbarrier.
-// Never used with .multicast::cluster.
+// Single-CTA destination: the box lands in this CTA's shared memory only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int c0, int c1) {
