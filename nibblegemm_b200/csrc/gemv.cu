@@ -496,8 +496,8 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
   if (static_cast<long long>(K) * N >= (1LL << 40)) return NG_ERR_BAD_SHAPE;
   if (splits < 0 || splits > 16) return NG_ERR_BAD_ARGUMENT;
   if (block_threads != 0 && block_threads != 128 && block_threads != 256) return NG_ERR_BAD_ARGUMENT;
-  if (algo < 0 || algo > 5) return NG_ERR_BAD_ARGUMENT;
-  if (algo >= 4 && (M > (algo == 5 ? 16 : 8) || splits > 8)) return NG_ERR_BAD_ARGUMENT;
+  if (algo < 0 || algo > 6) return NG_ERR_BAD_ARGUMENT;
+  if (algo >= 4 && algo <= 5 && (M > (algo == 5 ? 16 : 8) || splits > 8)) return NG_ERR_BAD_ARGUMENT;
   if (x_dtype == NG_DTYPE_BF16 && algo == 1) return NG_ERR_BAD_ARGUMENT;
   if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2) ||
       !aligned(workspace, 256))
@@ -541,6 +541,12 @@ extern "C" int ng_gemv_w4a16(const void* x, int x_dtype, const int32_t* qweight,
     } else if (M > 4 || (M >= 3 && wbytes >= 12.0 * (1 << 20))) {  // includes M = 9..16
       algo = 5;
     }
+  }
+  if (algo == 6) {
+    if (gemv_stream_supported(N, s))
+      return gemv_stream(x, x_dtype, q, s, y, M, K, N, group_size, splits, dev, strm);
+    algo = 5;  // scales without a 16-byte row stride: the ring streams them itself
+    if (splits > 8) splits = 8;
   }
   if (algo >= 4)
     return gemv_ring(x, x_dtype, algo == 5, q, s, y, M, K, N, group_size, splits, workspace,

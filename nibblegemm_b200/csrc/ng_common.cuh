@@ -133,6 +133,13 @@ int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void
             int N, int G, void* ws, const DeviceInfo& dev, cudaStream_t strm);
 
 
+// Bulk-copy tensor-pipe GEMV (gemv_stream.cu), M <= 16; arguments already
+// validated.  splits = cluster size (0 = heuristic).  Needs
+// gemv_stream_supported (N % 8 == 0, 16-byte aligned scales).
+bool gemv_stream_supported(int N, const void* scales);
+int gemv_stream(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M,
+                int K, int N, int G, int splits, const DeviceInfo& dev, cudaStream_t strm);
+
 // Bulk-copy ring GEMV (gemv_ring.cu), M <= 8; arguments already validated.
 int gemv_ring(const void* x, int x_dtype, bool tensor_pipe, const uint32_t* q, const __half* s,
               void* y, int M, int K, int N, int G, int splits, void* ws, size_t ws_bytes,

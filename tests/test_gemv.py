@@ -286,3 +286,74 @@ def test_wide_shapes_default_routing(K, N, M):
     y = ng.gemv(X, qw)
     check(y, ref, torch.float16)
     assert torch.equal(y, ng.gemv(X, qw, algo=5))
+
+
+# ---------------------------------------------------------------------------
+# Register-streamed tensor-pipe schedule (algo 6, M <= 16)
+# ---------------------------------------------------------------------------
+STREAM_CASES = [(1, 512, 256), (2, 256, 132), (3, 1024, 260), (4, 512, 512), (5, 2048, 132),
+                (8, 512, 256), (1, 320 * 4, 1024), (2, 256, 4), (7, 8192, 388), (9, 1024, 388),
+                (13, 2048, 132), (16, 512, 1028), (16, 4096, 4096)]
+
+
+@pytest.mark.parametrize("M,K,N", STREAM_CASES)
+@pytest.mark.parametrize("G", [64, 128, 256])
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+def test_stream_matches_oracle(M, K, N, G, act):
+    if K % G:
+        pytest.skip("K not a multiple of G")
+    X, qw, ref = make_case(M, K, N, G, seed=M * 7 + N + G, act=act)
+    check(ng.gemv(X, qw, algo=6), ref, X.dtype)
+    assert ng.extension().device_status() == 0
+
+
+@pytest.mark.parametrize("K,N", FULL + [(2048, 4096), (4096, 3072), (4096, 7168), (7168, 4096),
+                                        (4096, 28672), (8192, 28672), (28672, 8192)])
+@pytest.mark.parametrize("M", [1, 4, 8, 16])
+def test_stream_full_size_shapes(K, N, M):
+    X, qw, ref = make_case(M, K, N, 128, seed=K + N + M)
+    check(ng.gemv(X, qw, algo=6), ref, torch.float16)
+    assert ng.extension().device_status() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 5, 8, 16])
+def test_stream_split_invariance(splits):
+    X, qw, ref = make_case(3, 4096, 1028, 128, seed=splits)
+    y = ng.gemv(X, qw, splits=splits, algo=6)
+    check(y, ref, torch.float16)
+    assert torch.equal(y, ng.gemv(X, qw, splits=splits, algo=6))
+
+
+@pytest.mark.parametrize("scale", [1e-4, 1.0, 300.0])
+@pytest.mark.parametrize("act", ["f16", "bf16"])
+def test_stream_activation_magnitudes(scale, act):
+    """The offsets removed per group (sum x * (offset + 8)) scale with X, so the
+    relative error must not depend on the activations' magnitude."""
+    x, q, s = qo.synthetic_case(4, 4096, 1024, group_size=128, seed=11, act="f16")
+    xf = x.astype(np.float32) * scale
+    qw = ng.QuantizedWeight(torch.from_numpy(q), torch.from_numpy(s), 128, 4096, 1024).to("cuda")
+    dt = torch.float16 if act == "f16" else torch.bfloat16
+    X = torch.from_numpy(xf).to(dt).cuda()
+    xr = X.float().cpu().numpy()
+    ref = xr @ qo.dequantize_np(q, s, 128, 4096).astype(np.float32)
+    check(ng.gemv(X, qw, algo=6), ref, dt)
+
+
+def test_stream_output_fully_written_and_back_to_back_in_graph():
+    cases = [make_case(1, K, N, 128, seed=K + N) for K, N in [(4096, 14336), (14336, 4096), (4096, 4100)]]
+    ext = ng.extension()
+    outs = [torch.full((1, qw.N), float("nan"), dtype=torch.float16, device="cuda") for _, qw, _ in cases]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for (X, qw, _), o in zip(cases, outs):
+                ext.gemv_w4a16(X, qw.qweight, qw.scales, 128, algo=6, out=o)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    for (_, _, ref), o in zip(cases, outs):
+        check(o, ref, torch.float16)
+    assert ext.device_status() == 0
