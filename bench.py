@@ -36,6 +36,7 @@ scaling, no collective on the data path).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import subprocess
@@ -380,29 +381,19 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
-def run_decode(args, wl, world, rank, local, dist):
-    """Tokens/s of the full Llama-3-8B decode step (BASELINE config 4; with
-    ``--workload decode70b`` the Llama-3-70B step of config 5: context 2048,
-    ``--batch`` sequences).
-
-    One step = one token through embedding, 32 layers (RMSNorm, fused q|k|v
-    GEMV, GQA attention with RoPE + KV append over 1024 cached positions, o GEMV,
-    all-reduce, RMSNorm, fused gate|up GEMV, SwiGLU, down GEMV, all-reduce),
-    final norm, fp16 lm_head and argmax; captured once in a CUDA graph and
-    replayed with the position held at 1023 (context 1024).  Strong scaling.
-    """
-    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL, Llama3Decoder
-    big = args.workload == "decode70b"
-    cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
-    ctx = 2048 if big else 1024
-    batch = args.batch
-    m = Llama3Decoder(cfg, batch=batch, max_ctx=ctx, rank=rank, world=world, reduce=args.reduce,
-                      wide_split=not args.no_wide_split)
+def measure_decode(cfg, ctx, batch, steps, warmup, world, rank, dist, reduce="peer", wide_split=True,
+                   local=0, sample_clocks=True):
+    """Device-timed tokens/s of one Llama-3 decode step (every rank runs its
+    tensor-parallel shard), plus the end-to-end figure with the token ids
+    crossing PCIe.  Returns a dict of raw figures (identical on every rank)."""
+    from nibblegemm_b200.decode_model import Llama3Decoder
+    m = Llama3Decoder(cfg, batch=batch, max_ctx=ctx, rank=rank, world=world, reduce=reduce,
+                      wide_split=wide_split)
     m.pos.fill_(ctx - 1)
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             m.step(advance=False)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
@@ -414,15 +405,16 @@ def run_decode(args, wl, world, rank, local, dist):
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        for _ in range(100):  # fixed count on every rank: the graph holds collectives
+    sampler = ClockSampler(local) if sample_clocks else contextlib.nullcontext()
+    with sampler as clocks:
+        for _ in range(50):  # fixed count on every rank: the graph holds collectives
             graph.replay()
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
         with torch.cuda.stream(stream):
             start.record(stream)
-            for _ in range(args.steps):
+            for _ in range(steps):
                 graph.replay()
             end.record(stream)
         torch.cuda.synchronize()
@@ -431,11 +423,11 @@ def run_decode(args, wl, world, rank, local, dist):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
-    per_ms = ms / args.steps
-    # e2e: the token id in from pinned host memory, the step (graph), the next id back
+    per_ms = ms / steps
+    # e2e: the token ids in from pinned host memory, the step (graph), the next ids back
     tok_host = torch.zeros(batch, dtype=torch.int64).pin_memory()
     out_host = torch.zeros(batch, dtype=torch.int64).pin_memory()
-    e2e_steps = max(3, min(args.steps, 50))
+    e2e_steps = max(3, min(steps, 50))
     if dist:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -453,15 +445,40 @@ def run_decode(args, wl, world, rank, local, dist):
         t = torch.tensor([e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = t.item()
+    status = m.ext.device_status()
+    kv = 2 * cfg["layers"] * ctx * m.hkv * cfg["head_dim"] * 2 * batch
+    nbytes = m.weight_bytes + m.lm_head.numel() * 2 + kv + cfg["hidden"] * 2 * batch
+    out = dict(per_ms=per_ms, e2e_ms=e2e_ms, nbytes=nbytes, launches=m.launches_per_step(),
+               clocks=clocks.summary() if sample_clocks else None, status=status)
+    del graph, m
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_decode(args, wl, world, rank, local, dist):
+    """Tokens/s of the full Llama-3-8B decode step (BASELINE config 4; with
+    ``--workload decode70b`` the Llama-3-70B step of config 5: context 2048,
+    ``--batch`` sequences).
+
+    One step = one token through embedding, 32 layers (RMSNorm, fused q|k|v
+    GEMV, GQA attention with RoPE + KV append over 1024 cached positions, o GEMV,
+    all-reduce, RMSNorm, fused gate|up GEMV, SwiGLU, down GEMV, all-reduce),
+    final norm, fp16 lm_head with the argmax fused in; captured once in a CUDA
+    graph and replayed with the position held at ctx - 1.  Strong scaling.
+    """
+    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL
+    big = args.workload == "decode70b"
+    cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
+    ctx = 2048 if big else 1024
+    batch = args.batch
+    r = measure_decode(cfg, ctx, batch, args.steps, args.warmup, world, rank, dist, args.reduce,
+                       not args.no_wide_split, local)
+    assert r["status"] == 0, "a kernel reported a bounded-wait timeout"
     if rank == 0:
         hbm, _, src = measured_peaks()
-        kv = 2 * cfg["layers"] * ctx * m.hkv * cfg["head_dim"] * 2 * batch
-        nbytes = m.weight_bytes + m.lm_head.numel() * 2 + kv + cfg["hidden"] * 2 * batch
+        per_ms, e2e_ms, nbytes = r["per_ms"], r["e2e_ms"], r["nbytes"]
         achieved = nbytes / (per_ms * 1e-3) / 1e9
-        # ours per layer: 4 GEMVs (2 with the RMSNorm folded in), 2 attention (RoPE + KV
-        # append folded in), SwiGLU (+2 peer all-reduces); then the final norm and 2 argmax
         L = cfg["layers"]
-        launches = L * 7 + 3 + (2 * L if (world > 1 and args.reduce == "peer") else 0)
         line = {
             "metric": METRIC, "value": round(1000.0 * batch / per_ms, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
@@ -471,15 +488,15 @@ def run_decode(args, wl, world, rank, local, dist):
                        "kv_heads": cfg["kv_heads"], "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
                        "context": ctx, "group_size": 128, "batch": batch, "parallelism": f"tp{world}",
                        "tp_reduce": (args.reduce if world > 1 else None),
-                       "l2": f"{nbytes / 1e9:.1f} GB read per step (>> L2)",
+                       "l2": f"{nbytes / 1e9:.1f} GB read per step per rank (>> L2)",
                        "timing": "one CUDA graph per step (every sequence advances one token), replayed `steps` times"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": None,
                          "peak_source": f"{src} copy bandwidth", "algorithmic_bytes_per_step_per_rank": nbytes},
             "e2e": {"value": round(1000.0 * batch / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * batch,
                     "d2h_bytes_per_step": 8 * batch, "path": "token ids in -> Llama3Decoder.step() graph -> next ids out"},
-            "gpu_launches": launches,
-            "clocks": clocks.summary(),
+            "gpu_launches": r["launches"],
+            "clocks": r["clocks"],
         }
         print(json.dumps(line), flush=True)
     if dist:
@@ -587,6 +604,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gemv")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp-decode", action="store_true",
+                    help="gemv workload: skip the tensor-parallel Llama-3-8B decode-step measurement")
     ap.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
                     help="tensor-parallel all-reduce of the step8b workload")
     ap.add_argument("--batch", type=int, default=1, help="sequences per step (decode8b, decode70b)")
@@ -723,6 +742,14 @@ def main():
     else:
         e2e_val = flops * e2e_steps * world / (e2e_ms * 1e-3) / 1e12
 
+    # ---- the sharded path at this N: the Llama-3-8B decode step, tensor-parallel ----
+    tp = None
+    if args.workload == "gemv" and not args.no_tp_decode:
+        from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL
+        tp = measure_decode(LLAMA3_8B_MODEL, 1024, 1, max(10, min(args.steps, 100)), 3, world, rank, dist,
+                            reduce=args.reduce, local=local, sample_clocks=(rank == 0))
+        assert tp["status"] == 0, "a decode-step kernel reported an error"
+
     if rank == 0:
         hbm, tf, src = measured_peaks()
         if args.workload == "gemv":
@@ -756,6 +783,19 @@ def main():
             "clocks": clocks.summary(),
             "us_per_step": round(per_ms * 1e3, 3),
         }
+        if tp is not None:
+            line["tp_decode8b"] = {
+                "metric": "Llama-3-8B INT4 g128 decode tokens/s (BASELINE config 4), batch 1, context 1024",
+                "value": round(1000.0 / tp["per_ms"], 2), "unit": "tok/s", "world": world,
+                "parallelism": f"tp{world}", "reduce": args.reduce if world > 1 else None,
+                "ms_per_token": round(tp["per_ms"], 4),
+                "e2e_tok_s": round(1000.0 / tp["e2e_ms"], 2),
+                "roofline_per_rank": {"bound": "hbm", "algorithmic_bytes": tp["nbytes"],
+                                      "achieved_gbs": round(tp["nbytes"] / (tp["per_ms"] * 1e-3) / 1e9, 1),
+                                      "frac": round(tp["nbytes"] / (tp["per_ms"] * 1e-3) / 1e9 / hbm, 4)},
+                "gpu_launches_per_token": tp["launches"], "clocks": tp["clocks"],
+                "timing": "device time of one CUDA-graph step, max over ranks; strong scaling (fixed model)",
+            }
         if not args.no_cpu_baseline:
             v, per, sample, cores = cpu_reference_sample(wl)
             if args.workload == "gemm":

@@ -42,6 +42,7 @@ extern "C" {
 #define NG_ERR_UNSUPPORTED_DEVICE 7 /* current device is not sm_100                    */
 #define NG_ERR_CUDA 8               /* another CUDA runtime/driver call failed         */
 #define NG_ERR_DEVICE_TIMEOUT 9     /* a kernel's bounded pipeline wait expired        */
+#define NG_ERR_BAD_INDEX 10         /* a kernel met an index (token id) outside its table */
 
 /* Activation / output element types. */
 #define NG_DTYPE_F16 0
@@ -55,8 +56,8 @@ const char* ng_status_string(int status);
 
 /*
  * Synchronise `stream`, then return NG_ERR_DEVICE_TIMEOUT if any kernel of this
- * library on the current device gave up on a bounded wait since the last call
- * (and clear that flag), NG_ERR_CUDA if the stream reports an error, else NG_OK.
+ * library on the current device gave up on a bounded wait since the last call,
+ * else NG_ERR_BAD_INDEX if one met an out-of-range index (and clear both flags), NG_ERR_CUDA if the stream reports an error, else NG_OK.
  * No counterpart in the reference (its kernels have no waits that can expire).
  */
 int ng_device_status(void* stream);
@@ -262,6 +263,37 @@ int ng_gemv_w4a16_rmsnorm(const void* x, const void* residual_in, void* residual
  * at zero.  Calls sharing it must not overlap on the GPU. */
 int ng_argmax(const void* logits, int dtype, int M, int V, long long index_offset,
               void* best_scratch, float* value, long long* index, void* stream);
+
+/*
+ * Output head of the decode step with the argmax fused into its epilogue (no
+ * counterpart in the reference, whose decode step stops at the projections,
+ * bench/bench_model.py:57-86): for every token m and vocabulary row v of the
+ * dense head weight [V, H] (dtype, row-major), logit = x[m] . weight[v] in
+ * fp32; keys[m] = max(keys[m], key(logit, index_offset + v)) where
+ *   key(l, i) = ((order-preserving bits of l) << 32 | (2^32 - 1 - i)) with the
+ *               sign bit flipped,
+ * a signed 64-bit value whose maximum is the largest logit and, among equal
+ * logits, the smallest index.  Keys combine across vocabulary shards (tensor-
+ * parallel ranks) with a MAX all-reduce of int64.  keys must hold LLONG_MIN
+ * before the first call (ng_embed_tokens re-arms them); logits [M, V] may be
+ * NULL, else it receives the logits rounded to dtype.  x [M, H]; H % 128 == 0,
+ * H <= 16384; M <= 64 (weights are re-read per 8 tokens).
+ */
+int ng_lm_head_argmax(const void* x, const void* weight, int dtype, int M, int V, int H,
+                      long long index_offset, void* logits, long long* keys, void* stream);
+/*
+ * Token embedding gather (no counterpart in the reference): out[m, :] =
+ * table[t, :] with t = tokens[m], or, when keys is not NULL, t = the index
+ * encoded in keys[m] by ng_lm_head_argmax (keys[m] is then reset to LLONG_MIN
+ * and t is written to tokens_out[m] if tokens_out is not NULL).  zero_out
+ * (may be NULL) [M, H] is zero-filled (the residual stream of a new step).
+ * A token outside [0, V) gives a zero row and sets the device error word
+ * (ng_device_status reports it).  out may be NULL (only the token ids are
+ * decoded).  H % 8 == 0.
+ */
+int ng_embed_tokens(const long long* tokens, long long* keys, long long* tokens_out,
+                    const void* table, int dtype, int M, int H, long long V, void* out,
+                    void* zero_out, void* stream);
 
 #ifdef __cplusplus
 }

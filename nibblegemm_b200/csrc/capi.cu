@@ -81,7 +81,7 @@ extern "C" int ng_device_status(void* stream) {
     const unsigned int zero = 0;
     if (cudaMemcpy(dev.err, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess)
       return NG_ERR_CUDA;
-    return NG_ERR_DEVICE_TIMEOUT;
+    return (word & ngb::kErrWaitTimeout) ? NG_ERR_DEVICE_TIMEOUT : NG_ERR_BAD_INDEX;
   }
   return NG_OK;
 }
@@ -98,6 +98,7 @@ extern "C" const char* ng_status_string(int status) {
     case NG_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case NG_ERR_CUDA: return "a CUDA runtime call failed";
     case NG_ERR_DEVICE_TIMEOUT: return "a kernel gave up on a bounded pipeline wait";
+    case NG_ERR_BAD_INDEX: return "a kernel met an index outside its table";
     default: return "unknown status";
   }
 }

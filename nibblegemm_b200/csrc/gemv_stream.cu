@@ -51,7 +51,6 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 
 #include "ng_decode.cuh"
@@ -151,7 +150,7 @@ __device__ __forceinline__ void stream_drain(uint64_t* bar, uint32_t parity, uns
 // warp, 4: 16 rows), so 4 P consumer warps + 1 producer warp.  Cluster = csize
 // CTAs along gridDim.y.
 template <bool BF16, int TT, int SPG, int P>
-__global__ void __launch_bounds__((4 * P + 1) * 32, 1)
+__global__ void __launch_bounds__((4 * P + 1) * 32, P == 2 ? 3 : 1)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmap_q,
                        const __grid_constant__ CUtensorMap tmap_s,
                        const unsigned short* __restrict__ x, unsigned short* __restrict__ y, int M,
@@ -159,6 +158,7 @@ __global__ void __launch_bounds__((4 * P + 1) * 32, 1)
   constexpr int kSConsumers = kSStrips * P;   // consumer warps
   constexpr int kSThreads = (kSConsumers + 1) * 32;
   constexpr int RPG = SPG * 4;                 // packed rows per group
+  constexpr int NCH = 2;                       // independent MMA chains per A tile
   constexpr int PR = kSStageRows / P;          // packed rows per stage part
   static_assert(PR % RPG == 0, "a stage part holds whole groups");
   constexpr int HG = PR / RPG;                 // groups per stage part
@@ -290,13 +290,13 @@ __global__ void __launch_bounds__((4 * P + 1) * 32, 1)
         const int lg = st * SGR + part * HG + i;   // group within the CTA's slice
         if (lg < ngc) {
           // [token tile][A tile][pair half]: four independent MMA chains per tile
-          float acc[TT][2][2][4];
+          float acc[TT][2][NCH][4];
 #pragma unroll
           for (int t = 0; t < TT; ++t)
 #pragma unroll
             for (int p = 0; p < 2; ++p)
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
+              for (int h = 0; h < NCH; ++h)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[t][p][h][e] = 0.f;
 #pragma unroll
@@ -318,10 +318,10 @@ __global__ void __launch_bounds__((4 * P + 1) * 32, 1)
               decode_operands<BF16>(words[2 * p], lo);
               decode_operands<BF16>(words[2 * p + 1], hi);
               mma16816<BF16>(acc[0][p][0], lo[0], hi[0], lo[1], hi[1], xa.x, xa.y);
-              mma16816<BF16>(acc[0][p][1], lo[2], hi[2], lo[3], hi[3], xa.z, xa.w);
+              mma16816<BF16>(acc[0][p][NCH - 1], lo[2], hi[2], lo[3], hi[3], xa.z, xa.w);
               if constexpr (TT == 2) {
                 mma16816<BF16>(acc[TT - 1][p][0], lo[0], hi[0], lo[1], hi[1], xb.x, xb.y);
-                mma16816<BF16>(acc[TT - 1][p][1], lo[2], hi[2], lo[3], hi[3], xb.z, xb.w);
+                mma16816<BF16>(acc[TT - 1][p][NCH - 1], lo[2], hi[2], lo[3], hi[3], xb.z, xb.w);
               }
             }
           }
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__((4 * P + 1) * 32, 1)
             for (int p = 0; p < 2; ++p) {
               float a[4];
 #pragma unroll
-              for (int e = 0; e < 4; ++e) a[e] = acc[t][p][0][e] + acc[t][p][1][e];
+              for (int e = 0; e < 4; ++e) a[e] = NCH == 2 ? acc[t][p][0][e] + acc[t][p][NCH - 1][e] : acc[t][p][0][e];
               tot[t][2 * p][0] = fmaf(sc[2 * p], a[0] - c0, tot[t][2 * p][0]);
               tot[t][2 * p][1] = fmaf(sc[2 * p], a[1] - c1, tot[t][2 * p][1]);
               tot[t][2 * p + 1][0] = fmaf(sc[2 * p + 1], a[2] - c0, tot[t][2 * p + 1][0]);
@@ -449,10 +449,7 @@ int run_stream(const void* x, const uint32_t* q, const __half* s, void* y, int M
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   });
-  // Ring depth: 3 stages (about half an SM) when the grid covers the SMs, so the
-  // next kernel's CTAs fit beside these; deeper when SMs stay free anyway.
-  int nstages = tiles * C <= dev.sm_count * 3 / 4 ? kSMaxStages : 3;
-  if (const char* e = getenv("NG_STREAM_STAGES")) nstages = std::max(2, std::min(kSMaxStages, atoi(e)));
+  int nstages = 3;  // measured: deeper rings (4-6 stages) are not faster
   while (nstages > 2 && stream_smem_bytes(M, NG, C, G, nstages) > 200 * 1024) --nstages;
   const size_t smem = stream_smem_bytes(M, NG, C, G, nstages);
   if (smem > 200 * 1024) return NG_ERR_BAD_SHAPE;
@@ -505,7 +502,6 @@ int stream_g(const void* x, const uint32_t* q, const __half* s, void* y, int M, 
   // must share an SM (or a group is 32 rows, G = 256).
   const int tiles = (N + kSCols - 1) / kSCols;
   int P = (tiles * C <= dev.sm_count && G <= 128) ? 4 : 2;
-  if (const char* e = getenv("NG_STREAM_P")) P = (atoi(e) == 4 && G <= 128) ? 4 : 2;
   if (G == 64)
     return P == 4 ? run_stream<BF16, TT, 2, 4>(x, q, s, y, M, K, N, C, dev, st)
                   : run_stream<BF16, TT, 2, 2>(x, q, s, y, M, K, N, C, dev, st);

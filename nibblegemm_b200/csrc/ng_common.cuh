@@ -101,6 +101,8 @@ __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
 // Kernels OR this code into the per-device error word (DeviceInfo::err, a
 // device address) when a bounded wait expires; ng_device_status reads it back.
 constexpr unsigned int kErrWaitTimeout = 1u;
+// ... and this one when an index (a token id) lies outside its table.
+constexpr unsigned int kErrBadIndex = 2u;
 
 }  // namespace ngb
 

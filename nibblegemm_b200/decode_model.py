@@ -59,8 +59,9 @@ class Llama3Decoder:
                  device: Optional[torch.device] = None, seed: int = 0,
                  dtype: torch.dtype = torch.float16, group_size: int = 128,
                  reduce: str = "peer", attn_splits: int = 32, fused_rope: bool = True,
-                 fused_norm: bool = True, wide_split: bool = True):
+                 fused_norm: bool = True, wide_split: bool = True, keep_logits: bool = True):
         self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
+        self.keep_logits = keep_logits  # write the (rounded) logits besides the fused argmax
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
         self.max_ctx, self.attn_splits, self.fused_rope = max_ctx, attn_splits, fused_rope
@@ -129,6 +130,7 @@ class Llama3Decoder:
         self.res = torch.zeros(B, H, device=dev, dtype=dtype)
         self.res2 = torch.zeros(B, H, device=dev, dtype=dtype)  # ping-pong partner (folded norms)
         self.xn = torch.empty(B, H, device=dev, dtype=dtype)
+        self.xemb = torch.empty(B, H, device=dev, dtype=dtype)
         self.qkv = torch.empty(B, (hq + 2 * hkv) * D, device=dev, dtype=dtype)
         self.q = torch.empty(B, hq * D, device=dev, dtype=dtype)
         self.attn = torch.empty(B, hq * D, device=dev, dtype=dtype)
@@ -137,9 +139,9 @@ class Llama3Decoder:
         self.act = torch.empty(B, inter, device=dev, dtype=dtype)
         self.down = torch.empty(B, H, device=dev, dtype=dtype)
         self.logits = torch.empty(B, self.v1 - self.v0, device=dev, dtype=dtype)
-        self.best_scratch = torch.zeros(B, dtype=torch.int64, device=dev)  # argmax keys, re-armed per call
-        self.best_val = torch.empty(B, dtype=torch.float32, device=dev)
-        self.best_idx = torch.empty(B, dtype=torch.int64, device=dev)
+        # Per-token argmax keys of the fused head (LLONG_MIN = empty; the token
+        # decode at the end of the step re-arms them).
+        self.keys = torch.full((B,), -(2 ** 63), dtype=torch.int64, device=dev)
         self.attn_ws = torch.empty(self.ext.lib.ng_attn_workspace_bytes(B, hq, attn_splits),
                                    dtype=torch.uint8, device=dev)
         self._peer = None
@@ -183,6 +185,15 @@ class Llama3Decoder:
                                            x.size(1), float(self.cfg["eps"]), self._stream()),
                    "rmsnorm")
 
+    def launches_per_step(self) -> int:
+        """Kernels of this library one ``step()`` launches (torch's own ops and
+        NCCL's are not counted)."""
+        L = len(self.w)
+        per_layer = 4 + (2 if self.fused_rope else 3) + 1  # 4 GEMVs, attention, SwiGLU
+        norms = sum(1 for w in self.w for k in ("qkv", "gu") if not (self.fused_norm and not self._wide(w[k])))
+        peer = 2 * L if self._peer is not None else 0
+        return L * per_layer + norms + peer + 1 + 1 + 1 + 1  # embed, final norm, head, token decode
+
     # -- the step ----------------------------------------------------------------
     def step(self, advance: bool = True) -> None:
         """One token per sequence at position ``self.pos``; ``advance=False``
@@ -190,9 +201,11 @@ class Llama3Decoder:
         cfg, D, B = self.cfg, self.cfg["head_dim"], self.batch
         lib, dt = self.ext.lib, _DT[self.dtype]
         torch.add(self.pos, 1, out=self.ctx)
-        x = torch.nn.functional.embedding(self.tokens, self.embed)
-        self.res.zero_()
-        delta = x
+        # embedding gather; the residual stream of the step starts at zero
+        _lib.check(lib.ng_embed_tokens(self.tokens.data_ptr(), None, None, self.embed.data_ptr(), dt, B,
+                                       cfg["hidden"], cfg["vocab"], self.xemb.data_ptr(), self.res.data_ptr(),
+                                       self._stream()), "embed_tokens")
+        delta = self.xemb
         # The residual stream lives in `res`; a folded norm writes h to the other
         # buffer of the pair and the stream moves there (fixed per model, so a
         # captured graph replays the same buffers).
@@ -236,17 +249,16 @@ class Llama3Decoder:
             self._allreduce(self.down)
             delta = self.down
         self._norm(delta, res, self.final_norm, self.xn)
-        torch.mm(self.xn, self.lm_head.t(), out=self.logits)
-        idx_out = self.tokens if self.world == 1 else self.best_idx
-        _lib.check(self.ext.lib.ng_argmax(self.logits.data_ptr(), _DT[self.dtype], B, self.v1 - self.v0,
-                                          self.v0, self.best_scratch.data_ptr(), self.best_val.data_ptr(),
-                                          idx_out.data_ptr(), self._stream()), "argmax")
-        if self.world > 1:
-            pair = torch.stack([self.best_val, self.best_idx.float()], 1)  # exact for indices < 2^24
-            allp = [torch.empty_like(pair) for _ in range(self.world)]
-            torch.distributed.all_gather(allp, pair)
-            allp = torch.stack(allp, 0)  # [world, B, 2]
-            best = allp[:, :, 0].argmax(dim=0)
-            self.tokens.copy_(allp[best, torch.arange(B, device=self.device), 1].long())
+        # fp16 lm_head with the argmax fused into its epilogue (vocab shard per rank)
+        _lib.check(lib.ng_lm_head_argmax(self.xn.data_ptr(), self.lm_head.data_ptr(), dt, B, self.v1 - self.v0,
+                                         cfg["hidden"], self.v0,
+                                         self.logits.data_ptr() if self.keep_logits else None,
+                                         self.keys.data_ptr(), self._stream()), "lm_head_argmax")
+        if self.world > 1:  # one MAX all-reduce of B int64 keys combines the vocabulary shards
+            torch.distributed.all_reduce(self.keys, op=torch.distributed.ReduceOp.MAX)
+        # next token ids out of the keys (which are re-armed for the next step)
+        _lib.check(lib.ng_embed_tokens(None, self.keys.data_ptr(), self.tokens.data_ptr(), self.embed.data_ptr(),
+                                       dt, B, cfg["hidden"], cfg["vocab"], None, None, self._stream()),
+                   "embed_tokens")
         if advance:
             self.pos.add_(1)

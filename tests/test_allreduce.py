@@ -120,11 +120,13 @@ def _ar_worker(rank, world, port, q):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_allreduce_two_gpus():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_allreduce(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_ar_worker, args=(r, 2, 29723, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ar_worker, args=(r, world, 29723 + world, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=150) for _ in procs]

@@ -108,7 +108,9 @@ def test_decoder_matches_fp32_restatement(batch, dtype, fused, sms):
         tol = 2e-2 if dtype == torch.float16 else 4e-2
         assert _rel(m.xn, xn_ref) <= tol, (step, _rel(m.xn, xn_ref))
         assert _rel(m.logits, logits_ref) <= tol, (step, _rel(m.logits, logits_ref))
-        assert torch.equal(m.tokens, m.logits.float().argmax(1))
+        # the fused argmax works on fp32 logits: the chosen token's rounded logit is the maximum
+        lg = m.logits.float()
+        assert torch.equal(lg.gather(1, m.tokens[:, None]).squeeze(1), lg.max(1).values)
     assert ng.extension().device_status() == 0
 
 
@@ -167,11 +169,13 @@ def _tp_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_decoder_tp2_generates_the_tp1_tokens():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decoder_tp_generates_the_tp1_tokens(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, 29741, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, 29741 + world, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = q.get(timeout=150)
@@ -227,3 +231,73 @@ def test_rmsnorm_folded_gemv_matches_separate_kernels(dtype, M, K, N):
     d = (y.float() - ref.float()).abs().max().item() / ref.float().abs().max().item()
     assert d < (1e-2 if code else 2e-3), d
     assert ext.device_status() == 0
+
+
+def _keys_to_tokens(keys, M):
+    ext = ng.extension()
+    tok = torch.empty(M, dtype=torch.int64, device="cuda")
+    table = torch.zeros(1, 8, dtype=torch.float16, device="cuda")
+    st = ext.lib.ng_embed_tokens(None, keys.data_ptr(), tok.data_ptr(), table.data_ptr(), 0, M, 8,
+                                 2 ** 31, None, None, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    return tok
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,V,H", [(1, 128256 // 8, 4096), (3, 1000, 512), (8, 37, 256), (11, 4099, 1024)])
+def test_lm_head_argmax_matches_fp32_and_rearms(dtype, M, V, H):
+    """The fused head: logits (rounded to dtype) against an fp32 torch
+    restatement, the argmax against the fp32 maximum (an index whose fp32
+    logit is within the fp32 summation-order noise of the maximum), a planted
+    clear winner exactly, and the keys re-armed by the token decode."""
+    ext = ng.extension()
+    g = torch.Generator().manual_seed(M * 7 + V)
+    x = torch.randn(M, H, generator=g).to(dtype).cuda()
+    w = (torch.randn(V, H, generator=g) * 0.02).to(dtype).cuda()
+    win = [(m * 997 + 5) % V for m in range(M)]
+    for m in range(M):
+        w[win[m]] = (x[m].float() * 0.05).to(dtype)  # a clear winner per token
+    keys = torch.full((M,), -(2 ** 63), dtype=torch.int64, device="cuda")
+    logits = torch.empty(M, V, dtype=dtype, device="cuda")
+    dt = 1 if dtype == torch.bfloat16 else 0
+    st = ext.lib.ng_lm_head_argmax(x.data_ptr(), w.data_ptr(), dt, M, V, H, 123, logits.data_ptr(),
+                                   keys.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    ref = x.float() @ w.float().t()
+    assert _rel(logits, ref) <= (4e-3 if dtype == torch.float16 else 8e-3)
+    tok = _keys_to_tokens(keys, M) - 123
+    assert tok.tolist() == win
+    assert int((keys != -(2 ** 63)).sum()) == 0  # re-armed
+    # without a planted winner: the chosen logit is the fp32 maximum up to summation noise
+    w2 = (torch.randn(V, H, generator=g) * 0.02).to(dtype).cuda()
+    st = ext.lib.ng_lm_head_argmax(x.data_ptr(), w2.data_ptr(), dt, M, V, H, 0, None, keys.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    tok = _keys_to_tokens(keys, M)
+    ref2 = x.float() @ w2.float().t()
+    chosen = ref2.gather(1, tok[:, None]).squeeze(1)
+    assert torch.all(chosen >= ref2.max(1).values - 1e-4 * ref2.abs().max())
+    assert ext.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_embed_tokens_gathers_zeroes_and_flags_bad_ids(dtype):
+    ext = ng.extension()
+    V, H, M = 1000, 4096, 5
+    table = torch.randn(V, H).to(dtype).cuda()
+    tokens = torch.tensor([0, 999, 17, 17, 500], dtype=torch.int64, device="cuda")
+    out = torch.empty(M, H, dtype=dtype, device="cuda")
+    res = torch.full((M, H), 3.0, dtype=dtype, device="cuda")
+    dt = 1 if dtype == torch.bfloat16 else 0
+    st = ext.lib.ng_embed_tokens(tokens.data_ptr(), None, None, table.data_ptr(), dt, M, H, V, out.data_ptr(),
+                                 res.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    assert torch.equal(out, table[tokens]) and int(res.count_nonzero()) == 0
+    assert ext.device_status() == 0
+    bad = torch.tensor([3, 1000], dtype=torch.int64, device="cuda")  # 1000 is outside the table
+    st = ext.lib.ng_embed_tokens(bad.data_ptr(), None, None, table.data_ptr(), dt, 2, H, V, out.data_ptr(),
+                                 None, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    assert ext.device_status() == 10  # NG_ERR_BAD_INDEX, reported once and cleared
+    assert ext.device_status() == 0
+    assert torch.equal(out[0], table[3]) and int(out[1].count_nonzero()) == 0

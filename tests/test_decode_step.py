@@ -82,12 +82,14 @@ def _tp_worker(rank, world, port, q, reduce):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("reduce,port", [("peer", 29711), ("nccl", 29713)])
-def test_tp2_matches_tp1(reduce, port):
+def test_tp_matches_tp1(world, reduce, port):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, reduce)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port + 10 * world, q, reduce)) for r in range(world)]
     for p in procs:
         p.start()
     errs = q.get(timeout=150)
