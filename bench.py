@@ -382,13 +382,13 @@ def run_reference(args, rank):
 
 
 def measure_decode(cfg, ctx, batch, steps, warmup, world, rank, dist, reduce="peer", wide_split=True,
-                   local=0, sample_clocks=True):
+                   local=0, sample_clocks=True, **model_kw):
     """Device-timed tokens/s of one Llama-3 decode step (every rank runs its
     tensor-parallel shard), plus the end-to-end figure with the token ids
     crossing PCIe.  Returns a dict of raw figures (identical on every rank)."""
     from nibblegemm_b200.decode_model import Llama3Decoder
     m = Llama3Decoder(cfg, batch=batch, max_ctx=ctx, rank=rank, world=world, reduce=reduce,
-                      wide_split=wide_split)
+                      wide_split=wide_split, **model_kw)
     m.pos.fill_(ctx - 1)
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
@@ -471,8 +471,18 @@ def run_decode(args, wl, world, rank, local, dist):
     cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
     ctx = 2048 if big else 1024
     batch = args.batch
+    kw = {}
+    if args.gemv_algo is not None:
+        kw["gemv_algo"] = args.gemv_algo
+    if args.attn_splits:
+        kw["attn_splits"] = args.attn_splits
+    if args.no_fused_norm:
+        kw["fused_norm"] = False
+    if args.fold is not None:
+        kw["fold_silu"] = "silu" in args.fold
+        kw["fold_attn"] = "attn" in args.fold
     r = measure_decode(cfg, ctx, batch, args.steps, args.warmup, world, rank, dist, args.reduce,
-                       not args.no_wide_split, local)
+                       not args.no_wide_split, local, **kw)
     assert r["status"] == 0, "a kernel reported a bounded-wait timeout"
     if rank == 0:
         hbm, _, src = measured_peaks()
@@ -609,6 +619,12 @@ def main():
     ap.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
                     help="tensor-parallel all-reduce of the step8b workload")
     ap.add_argument("--batch", type=int, default=1, help="sequences per step (decode8b, decode70b)")
+    ap.add_argument("--gemv-algo", type=int, default=None,
+                    help="decode workloads: one ng_gemv_w4a16 algo for every projection")
+    ap.add_argument("--attn-splits", type=int, default=0, help="decode workloads: context splits")
+    ap.add_argument("--no-fused-norm", action="store_true", help="decode workloads: separate RMSNorm kernels")
+    ap.add_argument("--fold", default=None, help="decode workloads: kernels folded into GEMV staging "
+                    "('silu', 'attn', 'silu,attn' or 'none'; default: the model's choice)")
     ap.add_argument("--no-wide-split", action="store_true",
                     help="decode workloads: keep wide projections on the cluster GEMV")
     ap.add_argument("--algo", type=int, default=0, help="GEMV schedule (see ng_gemv_w4a16)")

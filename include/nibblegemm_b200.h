@@ -240,7 +240,9 @@ int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache, cons
 /* ng_rope_append + ng_attn_decode in one pass over the cache: q / K / V are
  * read from qkv [M, (Hq + 2 Hkv) * D], the new K / V row is written at pos[m]
  * (if inside the cache) by the chunk that reads it, and the context is
- * min(pos[m] + 1, max_ctx) rows. */
+ * min(pos[m] + 1, max_ctx) rows.  out == NULL: only the split partials are
+ * written to the workspace (layout [M][Hq][splits][2 + 128] fp32: running
+ * max, sum of exponentials, unnormalised output), for ng_gemv_w4a16_attn. */
 int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache, const int* pos, void* out,
                         int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,
                         float scale, float theta, void* workspace, size_t workspace_bytes,
@@ -257,6 +259,21 @@ int ng_gemv_w4a16_rmsnorm(const void* x, const void* residual_in, void* residual
                           const void* norm_weight, float eps, int x_dtype, const int32_t* qweight,
                           const uint16_t* scales, void* y, int M, int K, int N, int group_size,
                           void* stream);
+/* The same cluster GEMV with the kernel that produces its input folded into
+ * the activation staging (no counterpart in the reference, whose decode step
+ * is projections only):
+ *   ng_gemv_w4a16_silu: X = silu(gate) * up (rounded to x_dtype, as
+ *     ng_silu_mul) from gate_up [M, 2K] = gate | up; the SwiGLU before `down`.
+ *   ng_gemv_w4a16_attn: X = the attention output combined from the split
+ *     partials of ng_attn_decode_rope(out = NULL) [M][K / 128][splits][130],
+ *     in split order, bit-identical to the combine of ng_attn_decode_rope.
+ * M <= 16; otherwise the arguments of ng_gemv_w4a16. */
+int ng_gemv_w4a16_silu(const void* gate_up, int x_dtype, const int32_t* qweight,
+                       const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                       void* stream);
+int ng_gemv_w4a16_attn(const float* partials, int splits, int x_dtype, const int32_t* qweight,
+                       const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                       void* stream);
 /* Row-wise argmax of logits [M, V] (ties: smallest index): value[m] (fp32) and
  * index[m] + index_offset (int64; the offset places a vocab shard).
  * best_scratch: M x 8 bytes, zero before the first call; each call leaves it

@@ -551,12 +551,13 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
                                    void* out, int dtype, int M, int Hq, int Hkv, int D, int max_ctx,
                                    int splits, float scale, float theta, void* workspace,
                                    size_t workspace_bytes, void* stream) {
-  if (!qkv || !k_cache || !v_cache || !pos || !out || !workspace) return NG_ERR_NULL_POINTER;
+  if (!qkv || !k_cache || !v_cache || !pos || !workspace) return NG_ERR_NULL_POINTER;
   if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
   if (D != kAttnD || M < 1 || Hkv < 1 || Hq % Hkv || max_ctx < 1) return NG_ERR_BAD_SHAPE;
   if (Hq / Hkv != 1 && Hq / Hkv != 2 && Hq / Hkv != 4 && Hq / Hkv != 8) return NG_ERR_BAD_SHAPE;
   if (splits < 1 || splits > 256) return NG_ERR_BAD_ARGUMENT;
   if (workspace_bytes < ng_attn_workspace_bytes(M, Hq, splits)) return NG_ERR_BAD_ARGUMENT;
+  if (out != nullptr && !aligned(out, 2)) return NG_ERR_MISALIGNED;
   auto st = static_cast<cudaStream_t>(stream);
   const int chunk = (max_ctx + splits - 1) / splits;
   const dim3 g1(Hkv, splits, M), g2(Hq, M);
@@ -576,10 +577,13 @@ extern "C" int ng_attn_decode_rope(const void* qkv, void* k_cache, void* v_cache
       default: return partial(bf, std::integral_constant<int, 8>{});
     }
   };
+  // out == NULL: partials only (a consumer such as ng_gemv_w4a16_attn combines them)
   if (dtype == NG_DTYPE_BF16) {
     if (int e = by_g(std::true_type{})) return e;
+    if (out == nullptr) return NG_OK;
     return launch_pdl(attn_combine_kernel<true>, g2, dim3(kAttnD), st, part, out, Hq, splits);
   }
   if (int e = by_g(std::false_type{})) return e;
+  if (out == nullptr) return NG_OK;
   return launch_pdl(attn_combine_kernel<false>, g2, dim3(kAttnD), st, part, out, Hq, splits);
 }

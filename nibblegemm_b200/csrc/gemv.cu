@@ -53,6 +53,15 @@ constexpr int kU = 8;       // packed rows per chunk
 constexpr int kWin = 4;     // half2 path: packed rows per fp16 accumulation window
 constexpr int kMaxCluster = 16;
 constexpr int kStageBudget = 160 * 1024;  // activation staging limit (bytes)
+constexpr int kAttnHeadDim = 128;         // head dimension of the folded attention combine
+
+// Shared-memory offset of the folded attention-combine weights: after the
+// staged activations / warp partials and the CTA's final sums.
+__host__ __device__ inline size_t na_attw_offset(int MT, int rows_per_cta, int esz, int warps) {
+  const size_t stage = static_cast<size_t>(MT) * rows_per_cta * 8 * esz;
+  const size_t red = static_cast<size_t>(warps) * MT * kCols * 4;
+  return (stage > red ? stage : red) + static_cast<size_t>(MT) * kCols * 4;
+}
 
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -70,11 +79,24 @@ enum Path { kHalf2 = 0, kFloat2 = 1 };
 // whole row (a few KB from L2); CTA (0, 0) writes res_out, which must not
 // alias res_in (the caller ping-pongs two residual buffers).  w == nullptr:
 // plain GEMV.
+//
+// Two more foldings replace the kernel that would produce X (mode):
+//   kStageSilu: X[m, k] = act(silu(g) * u) with g = src[m, k], u = src[m, K + k]
+//     of the gate|up projection's output [M, 2K] (the SwiGLU before `down`);
+//   kStageAttn: X[m, h * 128 + d] = the split-context attention partials
+//     part[m][h][s] = (max_s, sum_s, o_s[128]) combined in split order,
+//     sum_s w_s o_s[d] / sum_s w_s sum_s with w_s = exp(max_s - max), exactly as
+//     the standalone combine kernel (the attention output before `o`).
+enum StageMode { kStagePlain = 0, kStageNorm = 1, kStageSilu = 2, kStageAttn = 3 };
+
 struct NormArgs {
   const unsigned short* res_in = nullptr;
   unsigned short* res_out = nullptr;
   const unsigned short* w = nullptr;
   float eps = 0.f;
+  int mode = kStagePlain;
+  const float* part = nullptr;  // kStageAttn: [M][K / 128][splits][2 + 128]
+  int splits = 0;
 };
 
 template <bool XBF16>
@@ -291,13 +313,70 @@ __global__ void __launch_bounds__(WARPS * 32)
     }
     __syncthreads();
   }
+  // ---- folded attention combine: per (token, head of the slice) split weights ----
+  const int h0 = (kr0 * 8) / kAttnHeadDim;
+  const int nh = nrows > 0 ? ((kr1 * 8 + kAttnHeadDim - 1) / kAttnHeadDim) - h0 : 0;
+  float* attw = nullptr;  // [MT][nh][splits + 1]: w_s, then the denominator
+  if (na.mode == kStageAttn) {
+    attw = reinterpret_cast<float*>(smem + na_attw_offset(MT, rows_per_cta, sizeof(XS), WARPS));
+    const int hq = K / kAttnHeadDim;
+    for (int i = tid; i < M * nh; i += WARPS * 32) {
+      const int m = i / nh, hl = i - m * nh;
+      const float* p = na.part + (static_cast<size_t>(m) * hq + h0 + hl) * na.splits * (2 + kAttnHeadDim);
+      float mx = -INFINITY;
+      for (int sp = 0; sp < na.splits; ++sp) mx = fmaxf(mx, p[sp * (2 + kAttnHeadDim)]);
+      float den = 0.f;
+      float* wv = attw + static_cast<size_t>(i) * (na.splits + 1);
+      for (int sp = 0; sp < na.splits; ++sp) {
+        const float ms = p[sp * (2 + kAttnHeadDim)];
+        const float w = ms == -INFINITY ? 0.f : __expf(ms - mx);  // empty split: weight 0
+        wv[sp] = w;
+        if (ms != -INFINITY) den += w * p[sp * (2 + kAttnHeadDim) + 1];
+      }
+      wv[na.splits] = den;
+    }
+    __syncthreads();
+  }
   // ---- stage X[:, kr0*8 : kr1*8) ------------------------------------------------
   for (int i = tid; i < MT * nrows; i += WARPS * 32) {
     const int m = i / nrows;
     const int r = i - m * nrows;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (m < M) v = ld_ro_v4(xin + static_cast<size_t>(m) * K + static_cast<size_t>(kr0 + r) * 8);
-    if (na.w != nullptr && m < M) {  // h = x + res_in, normalised, rounded to the activation type
+    const size_t k0 = static_cast<size_t>(kr0 + r) * 8;
+    if (m < M && (na.mode == kStagePlain || na.mode == kStageNorm))
+      v = ld_ro_v4(xin + static_cast<size_t>(m) * K + k0);
+    if (m < M && na.mode == kStageSilu) {  // act(silu(gate) * up), as the SwiGLU kernel rounds it
+      float gt[8], up[8];
+      unpack8<XBF16>(ld_ro_v4(xin + static_cast<size_t>(m) * 2 * K + k0), gt);
+      unpack8<XBF16>(ld_ro_v4(xin + static_cast<size_t>(m) * 2 * K + K + k0), up);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gt[j] = gt[j] / (1.f + __expf(-gt[j])) * up[j];
+      v = pack8<XBF16>(gt);
+    }
+    if (m < M && na.mode == kStageAttn) {  // combine the splits in split order
+      const int head = static_cast<int>(k0 / kAttnHeadDim);
+      const int d0 = static_cast<int>(k0 % kAttnHeadDim);
+      const float* wv = attw + (static_cast<size_t>(m) * nh + (head - h0)) * (na.splits + 1);
+      const float* p = na.part + (static_cast<size_t>(m) * (K / kAttnHeadDim) + head) * na.splits * (2 + kAttnHeadDim) + 2 + d0;
+      float num[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int sp = 0; sp < na.splits; ++sp) {
+        const float w = wv[sp];
+        if (w == 0.f) continue;
+        // a record is 130 floats: 8-byte aligned (d0 is a multiple of 8), not 16
+        const float2* o = reinterpret_cast<const float2*>(p + static_cast<size_t>(sp) * (2 + kAttnHeadDim));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 t = o[j];
+          num[2 * j] += w * t.x;
+          num[2 * j + 1] += w * t.y;
+        }
+      }
+      const float den = wv[na.splits];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) num[j] = num[j] / den;
+      v = pack8<XBF16>(num);
+    }
+    if (na.mode == kStageNorm && m < M) {  // h = x + res_in, normalised, rounded to the activation type
       float a[8], b[8], wf[8];
       unpack8<XBF16>(v, a);
       unpack8<XBF16>(ld_ro_v4(na.res_in + static_cast<size_t>(m) * K + static_cast<size_t>(kr0 + r) * 8), b);
@@ -444,7 +523,12 @@ int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int 
   if (static_cast<long long>(rows_per_cta) * MT * 8 * esz > kStageBudget) return NG_ERR_BAD_SHAPE;
   const size_t stage = static_cast<size_t>(MT) * rows_per_cta * 8 * esz;
   const size_t red = static_cast<size_t>(WARPS) * MT * kCols * 4;
-  const size_t smem = std::max(stage, red) + static_cast<size_t>(MT) * kCols * 4;
+  size_t smem = std::max(stage, red) + static_cast<size_t>(MT) * kCols * 4;
+  if (na.mode == kStageAttn) {  // split weights of the heads a slice touches
+    const int nh = (rows_per_cta * 8 + kAttnHeadDim - 1) / kAttnHeadDim + 1;
+    smem = na_attw_offset(MT, rows_per_cta, esz, WARPS) + static_cast<size_t>(MT) * nh * (na.splits + 1) * 4;
+    if (smem > 200 * 1024) return NG_ERR_BAD_SHAPE;
+  }
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(col_tiles, C, 1);
@@ -587,10 +671,60 @@ extern "C" int ng_gemv_w4a16_rmsnorm(const void* x, const void* residual_in, voi
   na.res_out = static_cast<unsigned short*>(residual_out);
   na.w = static_cast<const unsigned short*>(norm_weight);
   na.eps = eps;
+  na.mode = kStageNorm;
   const auto* q = reinterpret_cast<const uint32_t*>(qweight);
   const auto* s = reinterpret_cast<const __half*>(scales);
   auto strm = static_cast<cudaStream_t>(stream);
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_m<true, kFloat2, 8>(x, q, s, y, M, K, N, group_size, 0, dev, strm, na);
   return dispatch_m<false, kHalf2, 8>(x, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+}
+
+extern "C" int ng_gemv_w4a16_silu(const void* gate_up, int x_dtype, const int32_t* qweight,
+                                  const uint16_t* scales, void* y, int M, int K, int N,
+                                  int group_size, void* stream) {
+  using namespace ngb;
+  if (!gate_up || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || K % 8 != 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (!aligned(gate_up, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  NormArgs na;
+  na.mode = kStageSilu;
+  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NG_DTYPE_BF16)
+    return dispatch_m<true, kFloat2, 8>(gate_up, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+  return dispatch_m<false, kHalf2, 8>(gate_up, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+}
+
+extern "C" int ng_gemv_w4a16_attn(const float* partials, int splits, int x_dtype,
+                                  const int32_t* qweight, const uint16_t* scales, void* y, int M,
+                                  int K, int N, int group_size, void* stream) {
+  using namespace ngb;
+  if (!partials || !qweight || !scales || !y) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || K % kAttnHeadDim != 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (splits < 1 || splits > 256) return NG_ERR_BAD_ARGUMENT;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (!aligned(partials, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  NormArgs na;
+  na.mode = kStageAttn;
+  na.part = partials;
+  na.splits = splits;
+  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NG_DTYPE_BF16)
+    return dispatch_m<true, kFloat2, 8>(partials, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+  return dispatch_m<false, kHalf2, 8>(partials, q, s, y, M, K, N, group_size, 0, dev, strm, na);
 }

@@ -59,9 +59,19 @@ class Llama3Decoder:
                  device: Optional[torch.device] = None, seed: int = 0,
                  dtype: torch.dtype = torch.float16, group_size: int = 128,
                  reduce: str = "peer", attn_splits: int = 32, fused_rope: bool = True,
-                 fused_norm: bool = True, wide_split: bool = True, keep_logits: bool = True):
+                 fused_norm: bool = True, wide_split: bool = True, keep_logits: bool = True,
+                 gemv_algo: Optional[int] = None, fold_act: bool = True,
+                 fold_silu: Optional[bool] = None, fold_attn: Optional[bool] = None):
         self.cfg, self.batch, self.rank, self.world, self.dtype = cfg, batch, rank, world, dtype
         self.keep_logits = keep_logits  # write the (rounded) logits besides the fused argmax
+        self.gemv_algo = gemv_algo      # None: per-shape choice below; else this ng_gemv_w4a16 algo everywhere
+        # SwiGLU folded into the down GEMV and the attention combine into the o GEMV
+        # (needs the fused RoPE + attention kernel, which can leave its partials)
+        # Measured in the Llama-3-8B step: the SwiGLU fold is neutral at batch 1 and a
+        # loss at batch 4; the combine fold is a loss (every column tile of o re-does
+        # the combine of its heads), so it is off unless asked for.
+        self.fold_silu = (fold_act and batch <= 2) if fold_silu is None else fold_silu
+        self.fold_attn = (False if fold_attn is None else fold_attn) and fused_rope
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.layers = layers if layers is not None else cfg["layers"]
         self.max_ctx, self.attn_splits, self.fused_rope = max_ctx, attn_splits, fused_rope
@@ -162,6 +172,8 @@ class Llama3Decoder:
         # shapes; larger batches and wide projections: the library's default
         # routing (tensor-pipe ring)
         algo = (2 if x.dtype == torch.bfloat16 else 1) if x.size(0) <= 4 and not self._wide(w) else 0
+        if self.gemv_algo is not None:
+            algo = self.gemv_algo
         self.ext.gemv_w4a16(x, w.qweight, w.scales, w.group_size, algo=algo, out=out)
 
     def _allreduce(self, t):
@@ -189,7 +201,10 @@ class Llama3Decoder:
         """Kernels of this library one ``step()`` launches (torch's own ops and
         NCCL's are not counted)."""
         L = len(self.w)
-        per_layer = 4 + (2 if self.fused_rope else 3) + 1  # 4 GEMVs, attention, SwiGLU
+        # 4 GEMVs; attention partials (+ combine unless folded into o; + RoPE kernel
+        # unless fused); SwiGLU unless folded into down
+        per_layer = 4 + 1 + (0 if self.fold_attn else 1) + (0 if self.fused_rope else 1) + \
+            (0 if self.fold_silu else 1)
         norms = sum(1 for w in self.w for k in ("qkv", "gu") if not (self.fused_norm and not self._wide(w[k])))
         peer = 2 * L if self._peer is not None else 0
         return L * per_layer + norms + peer + 1 + 1 + 1 + 1  # embed, final norm, head, token decode
@@ -225,7 +240,8 @@ class Llama3Decoder:
             if self.fused_rope:  # RoPE + KV append inside the attention kernel
                 _lib.check(lib.ng_attn_decode_rope(
                     self.qkv.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
-                    self.pos.data_ptr(), self.attn.data_ptr(), dt, B, self.hq, self.hkv, D,
+                    self.pos.data_ptr(), None if self.fold_attn else self.attn.data_ptr(), dt, B,
+                    self.hq, self.hkv, D,
                     self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D), float(cfg["rope_theta"]),
                     self.attn_ws.data_ptr(), self.attn_ws.numel(), self._stream()), "attn_decode_rope")
             else:
@@ -240,12 +256,25 @@ class Llama3Decoder:
                                               self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D),
                                               self.attn_ws.data_ptr(), self.attn_ws.numel(),
                                               self._stream()), "attn_decode")
-            self._gemv(self.attn, w["o"], self.o)
+            if self.fold_attn:  # o projection with the attention combine in its staging
+                wo = w["o"]
+                _lib.check(lib.ng_gemv_w4a16_attn(self.attn_ws.data_ptr(), self.attn_splits, dt,
+                                                  wo.qweight.data_ptr(), wo.scales.data_ptr(),
+                                                  self.o.data_ptr(), B, wo.K, wo.N, wo.group_size,
+                                                  self._stream()), "gemv_w4a16_attn")
+            else:
+                self._gemv(self.attn, w["o"], self.o)
             self._allreduce(self.o)
             norm_proj(self.o, w["mlp_norm"], w["gu"], self.gu)
-            _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
-                                       self._stream()), "silu_mul")
-            self._gemv(self.act, w["down"], self.down)
+            if self.fold_silu:  # down projection with SwiGLU in its staging
+                wd = w["down"]
+                _lib.check(lib.ng_gemv_w4a16_silu(self.gu.data_ptr(), dt, wd.qweight.data_ptr(),
+                                                  wd.scales.data_ptr(), self.down.data_ptr(), B, wd.K,
+                                                  wd.N, wd.group_size, self._stream()), "gemv_w4a16_silu")
+            else:
+                _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
+                                           self._stream()), "silu_mul")
+                self._gemv(self.act, w["down"], self.down)
             self._allreduce(self.down)
             delta = self.down
         self._norm(delta, res, self.final_norm, self.xn)

@@ -87,10 +87,11 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("batch", [1, 3])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("fused,sms", [(True, None), (False, None), (True, 14), (True, 1)])
-def test_decoder_matches_fp32_restatement(batch, dtype, fused, sms):
+@pytest.mark.parametrize("fused,sms,fold", [(True, None, True), (True, None, False), (False, None, True),
+                                             (True, 14, True), (True, 1, True)])
+def test_decoder_matches_fp32_restatement(batch, dtype, fused, sms, fold):
     m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4, fused_rope=fused,
-                      fused_norm=fused)
+                      fused_norm=fused, fold_act=fold)
     if sms is not None:
         # pretend a smaller GPU: 14 SMs makes only gate|up (16 column tiles)
         # "wide" (separate norm + split ring, the residual stream changes buffer
@@ -301,3 +302,54 @@ def test_embed_tokens_gathers_zeroes_and_flags_bad_ids(dtype):
     assert ext.device_status() == 10  # NG_ERR_BAD_INDEX, reported once and cleared
     assert ext.device_status() == 0
     assert torch.equal(out[0], table[3]) and int(out[1].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,K,N", [(1, 14336, 4096), (3, 1792, 4096), (16, 512, 1028)])
+def test_silu_folded_gemv_is_bit_identical_to_separate_kernels(dtype, M, K, N):
+    ext = ng.extension()
+    dt = 1 if dtype == torch.bfloat16 else 0
+    g = torch.Generator().manual_seed(M + K)
+    gu = torch.randn(M, 2 * K, generator=g).to(dtype).cuda()
+    qw = ng.quantize(torch.randn(K, N, generator=g) * 0.02, 128).to("cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    act = torch.empty(M, K, dtype=dtype, device="cuda")
+    assert ext.lib.ng_silu_mul(gu.data_ptr(), act.data_ptr(), dt, M, K, st) == 0
+    y_ref = ext.gemv_w4a16(act, qw.qweight, qw.scales, 128, algo=2 if dt else 1)
+    y = torch.empty(M, N, dtype=dtype, device="cuda")
+    assert ext.lib.ng_gemv_w4a16_silu(gu.data_ptr(), dt, qw.qweight.data_ptr(), qw.scales.data_ptr(),
+                                      y.data_ptr(), M, K, N, 128, st) == 0
+    assert torch.equal(y, y_ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,hq,hkv,ctx,splits,pos", [(1, 32, 8, 1024, 32, 1023), (2, 8, 2, 64, 4, 5),
+                                                   (3, 4, 4, 40, 7, 39)])
+def test_attn_folded_gemv_is_bit_identical_to_combine_then_gemv(dtype, M, hq, hkv, ctx, splits, pos):
+    """The o projection with the split combine in its staging equals the
+    attention kernel's own combine followed by the plain GEMV, bit for bit;
+    pos < ctx - 1 leaves trailing splits empty."""
+    ext = ng.extension()
+    dt = 1 if dtype == torch.bfloat16 else 0
+    D = 128
+    g = torch.Generator().manual_seed(M * 13 + hq)
+    qkv = torch.randn(M, (hq + 2 * hkv) * D, generator=g).to(dtype).cuda()
+    kc = torch.randn(M, ctx, hkv, D, generator=g).to(dtype).cuda()
+    vc = torch.randn(M, ctx, hkv, D, generator=g).to(dtype).cuda()
+    posd = torch.full((M,), pos, dtype=torch.int32, device="cuda")
+    ws = torch.empty(ext.lib.ng_attn_workspace_bytes(M, hq, splits), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    out = torch.empty(M, hq * D, dtype=dtype, device="cuda")
+    args = lambda o, k, v: (qkv.data_ptr(), k.data_ptr(), v.data_ptr(), posd.data_ptr(), o, dt, M, hq, hkv, D,
+                            ctx, splits, 1.0 / math.sqrt(D), 500000.0, ws.data_ptr(), ws.numel(), st)
+    kc2, vc2 = kc.clone(), vc.clone()
+    assert ext.lib.ng_attn_decode_rope(*args(out.data_ptr(), kc, vc)) == 0
+    K, N = hq * D, 1024
+    qw = ng.quantize(torch.randn(K, N, generator=g) * 0.02, 128).to("cuda")
+    y_ref = ext.gemv_w4a16(out, qw.qweight, qw.scales, 128, algo=2 if dt else 1)
+    assert ext.lib.ng_attn_decode_rope(*args(None, kc2, vc2)) == 0
+    y = torch.empty(M, N, dtype=dtype, device="cuda")
+    assert ext.lib.ng_gemv_w4a16_attn(ws.data_ptr(), splits, dt, qw.qweight.data_ptr(), qw.scales.data_ptr(),
+                                      y.data_ptr(), M, K, N, 128, st) == 0
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert torch.equal(y, y_ref)
