@@ -5,7 +5,8 @@ same ops (``gemv_w4a16`` / ``gemm_w4a16`` / ``dequant_w4`` via ``extension()``),
 the same Python names, the same ``QuantLinear`` -- with hand-written sm_100a
 kernels behind a C ABI (``include/nibblegemm_b200.h``).
 """
-from .ops import DECODE_MAX_M, QuantLinear, dequant, extension, gemm, gemv, matmul
+from .ops import (DECODE_MAX_M, QuantLinear, check_device, dequant, dequantize, extension, gemm, gemv,
+                  matmul, reference_matmul, set_debug_checks)
 from .decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL, Llama3Decoder
 from .importers import from_autogptq, to_autogptq
 from .quant import QuantizedWeight, pack_nibbles, quantize, unpack_nibbles
@@ -19,7 +20,11 @@ __all__ = [
     "DECODE_MAX_M",
     "QuantLinear",
     "QuantizedWeight",
+    "check_device",
     "dequant",
+    "dequantize",
+    "reference_matmul",
+    "set_debug_checks",
     "extension",
     "gemm",
     "gemv",

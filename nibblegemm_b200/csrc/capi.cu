@@ -11,7 +11,7 @@ namespace {
 // One word per device (each device that loads the module has its own copy).
 __device__ unsigned int g_error_word;
 
-constexpr int kMaxDevices = 64;
+
 DeviceInfo g_info[kMaxDevices];
 std::once_flag g_once[kMaxDevices];
 int g_status[kMaxDevices];

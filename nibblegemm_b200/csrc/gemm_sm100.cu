@@ -390,7 +390,7 @@ int run_gemm(const void* x, const int32_t* q, const __half* s, void* y, int M, i
   int stages = std::min(16, (kSmemBudget - 1024 - static_cast<int>(sizeof(Barriers))) / stage_bytes);
   const size_t smem = 1024 + static_cast<size_t>(stages) * stage_bytes + sizeof(Barriers);
   auto kern = gemm_kernel<BT, BF16>;
-  static std::once_flag once[64];
+  static std::once_flag once[kMaxDevices];
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 4096);
   });

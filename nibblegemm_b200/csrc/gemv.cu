@@ -486,8 +486,8 @@ int run(const void* x, const uint32_t* qw, const __half* s, void* y, int M, int 
   const int col_tiles = (N + kCols - 1) / kCols;
 
   // Per-device one-time attribute set-up for this instantiation.
-  static std::once_flag once[64];
-  static int occ_cache[64];
+  static std::once_flag once[kMaxDevices];
+  static int occ_cache[kMaxDevices];
   const int d = dev.device;
   std::call_once(once[d], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

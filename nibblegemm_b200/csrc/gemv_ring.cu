@@ -950,7 +950,7 @@ int run_ring(const void* x, const uint32_t* qw, const __half* s, void* y, int M,
   const int sms = dev.sm_count;
   const size_t smem_cap = dev.smem_optin ? dev.smem_optin : 227 * 1024;
 
-  static std::once_flag once[64];
+  static std::once_flag once[kMaxDevices];
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem_cap));
@@ -1119,7 +1119,7 @@ int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int
   if (smem > smem_cap) return -1;
 
   auto kern = gemv_ring_sk_kernel<MT, XBF16>;
-  static std::once_flag once[64];
+  static std::once_flag once[kMaxDevices];
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_cap));
   });
@@ -1144,13 +1144,16 @@ int run_ring_sk(const void* x, const uint32_t* qw, const __half* s, void* y, int
   cfg.blockDim = dim3(kSkThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  // Not a cooperative launch: the grid is at most one CTA per SM and every
-  // wait is bounded, and a cooperative launch was measured to gain nothing.
-  cudaLaunchAttribute attr[1];
+  // Cooperative: a tile's finisher waits for the CTAs holding its other blocks,
+  // so every CTA must be resident at once; the launch fails (no hang) when they
+  // cannot be, e.g. while another kernel holds the SMs.
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return launch_status(cudaLaunchKernelEx(&cfg, kern, tmap, x, s, y, M, K, N, G, plan, stages,
                                           sc_groups, ws_part, ws_flag, dev.err));
 }

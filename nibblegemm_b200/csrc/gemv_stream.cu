@@ -444,7 +444,7 @@ int run_stream(const void* x, const uint32_t* q, const __half* s, void* y, int M
   constexpr int G = RPG * 8;
   const int NG = K / G;
   const int tiles = (N + kSCols - 1) / kSCols;
-  static std::once_flag once[64];
+  static std::once_flag once[kMaxDevices];
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);

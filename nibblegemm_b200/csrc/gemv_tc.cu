@@ -407,8 +407,8 @@ int run_tc(const void* x, const uint32_t* q, const __half* s, void* y, int M, in
            void* ws, const DeviceInfo& dev, cudaStream_t stream) {
   auto kern = gemv_tc_kernel<NT, GS, XBF16>;
   constexpr size_t smem = TcSmem<NT, GS>::kBytes;
-  static std::once_flag once[64];
-  static int resident[64];
+  static std::once_flag once[kMaxDevices];
+  static int resident[kMaxDevices];
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     int occ = 0;
@@ -493,9 +493,9 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 // Device address of g_noalloc_scratch on each device.  In host code the
 // array's name is only a host-side stand-in, so the address is looked up with
 // cudaGetSymbolAddress, once per device, with that device current.
-void* g_noalloc_ptr[64];
-int g_noalloc_status[64];
-std::once_flag g_noalloc_once[64];
+void* g_noalloc_ptr[kMaxDevices];
+int g_noalloc_status[kMaxDevices];
+std::once_flag g_noalloc_once[kMaxDevices];
 
 }  // namespace
 }  // namespace ngb

@@ -233,7 +233,7 @@ extern "C" int ng_lm_head_argmax(const void* x, const void* weight, int dtype, i
   auto* ls = static_cast<unsigned short*>(logits);
   const size_t smem = 8 * static_cast<size_t>(H * 2 + 64) + kHWarps * 8 * sizeof(long long);
   auto kern = dtype == NG_DTYPE_BF16 ? lm_head_kernel<true> : lm_head_kernel<false>;
-  static std::once_flag once[64];
+  static std::once_flag once[kMaxDevices];
   std::call_once(once[dev.device], [&] {
     cudaFuncSetAttribute(lm_head_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(lm_head_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -111,6 +111,10 @@ constexpr unsigned int kErrBadIndex = 2u;
 // ---------------------------------------------------------------------------
 namespace ngb {
 
+// Per-device host state (property cache, one-time kernel attributes) is held in
+// arrays of this many entries; current_device_info rejects larger ordinals.
+constexpr int kMaxDevices = 64;
+
 struct DeviceInfo {
   int device = -1;
   int sm_count = 0;

@@ -16,6 +16,7 @@ reference does.  There is no CPU path: tensors must be on a CUDA device.
 from __future__ import annotations
 
 import contextlib
+import os
 from typing import Optional
 
 import torch
@@ -27,6 +28,31 @@ from .quant import QuantizedWeight, quantize  # noqa: F401  (re-exported)
 DECODE_MAX_M = 8
 
 _DTYPE_CODE = {torch.float16: _lib.NG_DTYPE_F16, torch.bfloat16: _lib.NG_DTYPE_BF16}
+
+
+#: When true, every op synchronises its stream after the launch and raises if a
+#: kernel reported a bounded-wait timeout or a bad index (see ``check_device``).
+#: Off by default: it costs a host synchronisation per call and cannot be used
+#: inside CUDA-graph capture.  Also enabled by ``NIBBLEGEMM_DEBUG=1``.
+DEBUG_CHECKS = os.environ.get("NIBBLEGEMM_DEBUG", "") not in ("", "0")
+
+
+def set_debug_checks(enabled: bool) -> None:
+    """Turn the per-op device-status check on or off."""
+    global DEBUG_CHECKS
+    DEBUG_CHECKS = bool(enabled)
+
+
+def check_device() -> None:
+    """Synchronise the current stream and raise ``NibbleError`` if a kernel of
+    this library gave up on a bounded wait (its output is then undefined) or met
+    an out-of-range index since the last check; clears the flag."""
+    _lib.check(extension().device_status(), "device status")
+
+
+def _after(op: str) -> None:
+    if DEBUG_CHECKS and not torch.cuda.is_current_stream_capturing():
+        _lib.check(extension().device_status(), op)
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -119,6 +145,7 @@ class _Extension:
                                         _DTYPE_CODE[out_dtype], K, N, int(group_size), int(bool(fast)),
                                         torch.cuda.current_stream().cuda_stream)
         _lib.check(st, "dequant_w4")
+        _after("dequant_w4")
         return out
 
     def gemv_w4a16(self, X: torch.Tensor, Wq: torch.Tensor, S: torch.Tensor, group_size: int,
@@ -140,6 +167,7 @@ class _Extension:
                                         int(threads_override), int(algo), ws.data_ptr(), ws.numel(),
                                         stream)
         _lib.check(st, "gemv_w4a16")
+        _after("gemv_w4a16")
         return y
 
     def gemm_w4a16(self, X: torch.Tensor, Wq: torch.Tensor, S: torch.Tensor, group_size: int,
@@ -155,6 +183,7 @@ class _Extension:
                                         S.data_ptr(), y.data_ptr(), M, K, N, int(group_size),
                                         int(tile_tokens), ws.data_ptr(), ws.numel(), stream)
         _lib.check(st, "gemm_w4a16")
+        _after("gemm_w4a16")
         return y
 
     def device_status(self) -> int:
@@ -178,6 +207,23 @@ def dequant(qw: QuantizedWeight, fast: bool = True, dtype: torch.dtype = torch.f
     return extension().dequant_w4(qw.qweight, qw.scales, qw.group_size, fast, out_dtype=dtype)
 
 
+def dequantize(qw: QuantizedWeight) -> torch.Tensor:
+    """The reference's ``dequantize``: dense fp16 ``[K, N]`` = (u - 8) * scale with
+    one rounding, on ``qw``'s device.  A CPU weight is expanded by the GPU kernel
+    on the current CUDA device and the result returned to the CPU (there is no
+    CPU implementation in this library)."""
+    if qw.qweight.is_cuda:
+        return dequant(qw)
+    return dequant(qw.to(torch.device("cuda", torch.cuda.current_device()))).cpu()
+
+
+def reference_matmul(X: torch.Tensor, qw: QuantizedWeight) -> torch.Tensor:
+    """The reference's accuracy yardstick: fp16(X.float() @ dequantize(qw).float()),
+    on X's device (dense fp32 product; slow, for checking, not serving)."""
+    W = dequantize(qw).to(X.device)
+    return (X.float() @ W.float()).to(torch.float16)
+
+
 def gemv(X: torch.Tensor, qw: QuantizedWeight, version: int = 4, splits: int = 0,
          block_threads: int = 0, algo: int = 0) -> torch.Tensor:
     """Decode-regime ``X @ dequant(qw)`` for 1 <= M <= 16.
@@ -197,42 +243,52 @@ def gemm(X: torch.Tensor, qw: QuantizedWeight, version: int = 6) -> torch.Tensor
 
 def matmul(X: torch.Tensor, qw: QuantizedWeight, splits: int = 0,
            block_threads: int = 0) -> torch.Tensor:
-    """``X @ dequant(qw)``, dispatching on batch size at ``DECODE_MAX_M``."""
+    """``X @ dequant(qw)`` routed by the number of rows of ``X``.
+
+    Up to ``DECODE_MAX_M`` rows the product is a bandwidth-bound GEMV (one pass
+    over the packed weight); beyond that it is a tensor-core GEMM.  ``splits`` and
+    ``block_threads`` reach the GEMV only.  Shape errors raise ``ValueError``.
+    """
     if X.dim() != 2:
-        raise ValueError(f"expected a 2-D activation matrix, got {tuple(X.shape)}")
-    if X.size(1) != qw.K:
-        raise ValueError(f"K mismatch: activations have {X.size(1)}, weights have {qw.K}")
-    if X.size(0) <= DECODE_MAX_M:
-        return gemv(X, qw, version=4, splits=splits, block_threads=block_threads)
-    return gemm(X, qw)
+        raise ValueError(f"matmul takes a 2-D [M, K] activation, not shape {tuple(X.shape)}")
+    rows, depth = X.shape
+    if depth != qw.K:
+        raise ValueError(f"activation depth {depth} does not match the weight's K = {qw.K}")
+    use_gemv = rows <= DECODE_MAX_M
+    return (gemv(X, qw, version=4, splits=splits, block_threads=block_threads) if use_gemv
+            else gemm(X, qw))
 
 
 class QuantLinear(torch.nn.Module):
-    """Drop-in ``nn.Linear`` with packed INT4 weights (reference ops.py:107-135).
+    """``nn.Linear`` replacement holding a packed INT4 weight.
 
-    Buffers ``qweight``, ``scales`` and ``bias`` keep the reference's names, so
-    state dicts move between the two libraries unchanged.
+    The state-dict entries are ``qweight`` ([K/8, N] int32), ``scales`` ([K/G, N]
+    fp16) and ``bias`` (optional), the names the reference library uses, so a
+    checkpoint of one loads into the other.  ``forward`` accepts any leading
+    shape ``[..., K]`` and returns ``[..., N]``.
     """
 
     def __init__(self, qw: QuantizedWeight, bias: Optional[torch.Tensor] = None):
         super().__init__()
-        self.register_buffer("qweight", qw.qweight)
-        self.register_buffer("scales", qw.scales)
-        self.register_buffer("bias", bias if bias is not None else None)
-        self.group_size, self.K, self.N = qw.group_size, qw.K, qw.N
+        self.K, self.N, self.group_size = qw.K, qw.N, qw.group_size
+        for name, t in (("qweight", qw.qweight), ("scales", qw.scales), ("bias", bias)):
+            self.register_buffer(name, t)
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear, group_size: int = 128) -> "QuantLinear":
-        # nn.Linear stores [out, in]; the kernels consume [in, out].
-        qw = quantize(linear.weight.data.t().contiguous(), group_size)
-        bias = linear.bias.data.clone() if linear.bias is not None else None
-        return cls(qw.to(linear.weight.device), bias)
+        """Quantise an existing layer (round-to-nearest, per-group scales)."""
+        weight_kn = linear.weight.detach().transpose(0, 1).contiguous()  # Linear keeps [N, K]
+        packed = quantize(weight_kn, group_size).to(linear.weight.device)
+        bias = None if linear.bias is None else linear.bias.detach().clone()
+        return cls(packed, bias)
 
-    def _qw(self) -> QuantizedWeight:
+    def packed(self) -> QuantizedWeight:
+        """The layer's weight as a :class:`QuantizedWeight` view of its buffers."""
         return QuantizedWeight(self.qweight, self.scales, self.group_size, self.K, self.N)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        shape = x.shape
-        y = matmul(x.reshape(-1, shape[-1]).contiguous(), self._qw())
-        y = y.reshape(*shape[:-1], self.N)
-        return y + self.bias if self.bias is not None else y
+        lead = x.shape[:-1]
+        out = matmul(x.reshape(-1, x.shape[-1]).contiguous(), self.packed()).view(*lead, self.N)
+        if self.bias is None:
+            return out
+        return out + self.bias

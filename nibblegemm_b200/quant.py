@@ -107,12 +107,11 @@ def pack_nibbles_torch(codes: torch.Tensor) -> torch.Tensor:
 def quantize(W: torch.Tensor, group_size: int = 128, clip_search: bool = False) -> QuantizedWeight:
     """Round-to-nearest symmetric INT4 of a ``[K, N]`` weight (reference quant.py:127-161).
 
-    Returns CPU tensors, like the reference.  ``clip_search`` is accepted for
-    signature compatibility; the MSE clip search is an offline quality option
-    outside this library's kernel path and is rejected if requested.
+    Returns CPU tensors, like the reference.  ``clip_search=True`` picks each
+    group's scale among clipped max-abs candidates by the smallest squared
+    reconstruction error (reference quant.py:81-125, off by default there too,
+    because lower weight error did not mean a better model).
     """
-    if clip_search:
-        raise NotImplementedError("clip_search is not provided by nibblegemm_b200")
     if W.ndim != 2:
         raise ValueError(f"expected a 2-D weight, got shape {tuple(W.shape)}")
     K, N = W.shape
@@ -120,10 +119,38 @@ def quantize(W: torch.Tensor, group_size: int = 128, clip_search: bool = False) 
         raise ValueError(f"K={K} must be divisible by group_size={group_size}")
     if group_size % PACK_FACTOR:
         raise ValueError(f"group_size={group_size} must be divisible by {PACK_FACTOR}")
-    return quantize_on_device(W, group_size).to("cpu")
+    return quantize_on_device(W, group_size, clip_search).to("cpu")
 
 
-def quantize_on_device(W: torch.Tensor, group_size: int = 128) -> QuantizedWeight:
+#: Clip ratios the scale search tries, largest first (the first of equally good
+#: candidates wins): 1.0, 0.975, ..., 0.55.
+CLIP_CANDIDATES = torch.linspace(1.0, 0.55, 19)
+
+
+def _clip_scales(w: torch.Tensor, cols_per_pass: int = 4096) -> torch.Tensor:
+    """Per-(group, column) scale of ``w`` [groups, G, N] minimising
+    sum((round(w / s) clamped to [-8, 7]) * s - w)^2 over the candidates
+    s = max|w| * r / 7; processed a column block at a time to bound memory."""
+    ng, _, N = w.shape
+    best = torch.empty(ng, N, dtype=w.dtype, device=w.device)
+    ratios = CLIP_CANDIDATES.to(w.device, w.dtype)
+    for c0 in range(0, N, cols_per_pass):
+        blk = w[:, :, c0:c0 + cols_per_pass]
+        amax = blk.abs().amax(dim=1)
+        pick = (amax / QMAX).clamp(min=1e-8)
+        pick_err = torch.full_like(amax, float("inf"))
+        for r in ratios:
+            s = (amax * r / QMAX).clamp(min=1e-8)
+            recon = torch.round(blk / s[:, None, :]).clamp(QMIN, QMAX) * s[:, None, :]
+            err = (recon - blk).square().sum(dim=1)
+            take = err < pick_err
+            pick = torch.where(take, s, pick)
+            pick_err = torch.where(take, err, pick_err)
+        best[:, c0:c0 + cols_per_pass] = pick
+    return best
+
+
+def quantize_on_device(W: torch.Tensor, group_size: int = 128, clip_search: bool = False) -> QuantizedWeight:
     """:func:`quantize` leaving the packed weight on ``W``'s device (the same RTN
     arithmetic, run by torch on a CUDA tensor: quantising a model's 224
     projections on the GPU takes seconds)."""
@@ -131,7 +158,7 @@ def quantize_on_device(W: torch.Tensor, group_size: int = 128) -> QuantizedWeigh
     if K % group_size or group_size % PACK_FACTOR:
         raise ValueError(f"K={K} / group_size={group_size} not supported")
     w = W.detach().float().reshape(K // group_size, group_size, N)
-    scale = (w.abs().amax(dim=1) / QMAX).clamp(min=1e-8)
+    scale = _clip_scales(w) if clip_search else (w.abs().amax(dim=1) / QMAX).clamp(min=1e-8)
     codes = (torch.round(w / scale.unsqueeze(1)).clamp(QMIN, QMAX) + ZERO_POINT).reshape(K, N)
     return QuantizedWeight(qweight=pack_nibbles_torch(codes).contiguous(),
                            scales=scale.to(torch.float16).contiguous(), group_size=group_size,

@@ -18,6 +18,8 @@ Cases (inputs are regenerated deterministically from the seeds in this file):
   ``tests/test_dequant.py:27-44`` with unit, 2**[-10, 10] and per-group 2**g
   scales, G in {64, 128}.
 * ``quant_*``  -- ``quantize`` (RTN) of seeded ``N(0,1)*0.02`` weights, G in {64, 128}.
+* ``clip_*``   -- ``quantize(clip_search=True)`` of seeded weights with planted
+  outliers (so clipped candidates win in some groups), G in {64, 128}.
 * ``mm_*``     -- ``reference_matmul`` on the BASELINE synthetic distribution
   (codes uniform 0..15, scales |N(0,1)|*0.02+1e-3, X ~ N(0,1)) at small shapes.
 """
@@ -112,6 +114,15 @@ def main() -> None:
         out[f"quant_g{G}_W"] = W.numpy()
         out[f"quant_g{G}_qweight"] = qw.qweight.numpy()
         out[f"quant_g{G}_scales"] = qw.scales.numpy()
+
+    for G in (64, 128):
+        g = torch.Generator().manual_seed(200 + G)
+        W = torch.randn(512, 40, generator=g) * 0.02
+        W[::37, ::3] *= 8.0  # outliers: the MSE search clips some groups
+        qw = ref.quantize(W, group_size=G, clip_search=True)
+        out[f"clip_g{G}_W"] = W.numpy()
+        out[f"clip_g{G}_qweight"] = qw.qweight.numpy()
+        out[f"clip_g{G}_scales"] = qw.scales.numpy()
 
     for M, K, N, G, seed in MM_CASES:
         codes, scales, x = mm_inputs(M, K, N, G, seed)

@@ -91,7 +91,7 @@ def _rel(a, b):
                                              (True, 14, True), (True, 1, True)])
 def test_decoder_matches_fp32_restatement(batch, dtype, fused, sms, fold):
     m = Llama3Decoder(TINY, batch=batch, max_ctx=64, dtype=dtype, attn_splits=4, fused_rope=fused,
-                      fused_norm=fused, fold_act=fold)
+                      fused_norm=fused, fold_silu=fold, fold_attn=fold)
     if sms is not None:
         # pretend a smaller GPU: 14 SMs makes only gate|up (16 column tiles)
         # "wide" (separate norm + split ring, the residual stream changes buffer
@@ -353,3 +353,41 @@ def test_attn_folded_gemv_is_bit_identical_to_combine_then_gemv(dtype, M, hq, hk
                                       y.data_ptr(), M, K, N, 128, st) == 0
     assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
     assert torch.equal(y, y_ref)
+
+
+FULL_WIDTH = dict(layers=2, hidden=4096, heads=32, kv_heads=8, head_dim=128, intermediate=14336,
+                  vocab=128256, rope_theta=500000.0, eps=1e-5)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float16, 5e-3), (torch.bfloat16, 2e-2)])
+def test_decoder_full_llama3_8b_widths_matches_fp32_restatement(dtype, tol):
+    """Two layers at the Llama-3-8B widths (the shapes that route through the
+    wide GEMV schedules and the 32-way context split), three teacher-forced
+    steps against the fp32 restatement: final hidden state and logits within
+    max|err|/max|ref| <= 5e-3 with fp16 activations (bf16 keeps 8 mantissa
+    bits, so its residual stream alone differs by ~4e-3 per rounding; 2e-2)."""
+    m = Llama3Decoder(FULL_WIDTH, batch=1, max_ctx=64, dtype=dtype)
+    ref = RefModel(m)
+    g = torch.Generator().manual_seed(7)
+    for step in range(3):
+        toks = torch.randint(0, FULL_WIDTH["vocab"], (1,), generator=g).cuda()
+        pos = m.pos.clone()
+        m.tokens.copy_(toks)
+        m.step()
+        torch.cuda.synchronize()
+        xn_ref, logits_ref = ref.step(toks, pos)
+        assert _rel(m.xn, xn_ref) <= tol, (step, _rel(m.xn, xn_ref))
+        assert _rel(m.logits, logits_ref) <= tol, (step, _rel(m.logits, logits_ref))
+    assert ng.extension().device_status() == 0
+
+
+@pytest.mark.parametrize("G", [64, 128])
+def test_quantize_on_device_matches_reference_golden(golden, G):
+    """RTN quantisation run on the GPU (how every projection of the decode
+    models is built) reproduces the reference's own quantize() bit for bit."""
+    from nibblegemm_b200.quant import quantize_on_device
+    W = torch.from_numpy(golden[f"quant_g{G}_W"]).cuda()
+    qw = quantize_on_device(W, G)
+    assert qw.qweight.is_cuda
+    assert torch.equal(qw.qweight.cpu(), torch.from_numpy(golden[f"quant_g{G}_qweight"]))
+    assert torch.equal(qw.scales.cpu(), torch.from_numpy(golden[f"quant_g{G}_scales"]))

@@ -136,3 +136,16 @@ def test_bf16_rounding_helper():
     got = qo.bf16_bits_to_f32(qo.f32_to_bf16_bits(vals))
     ref = torch.from_numpy(vals).to(torch.bfloat16).float().numpy()
     assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("G", [64, 128])
+def test_quantize_clip_search_matches_reference_golden(golden, G):
+    """quantize(clip_search=True): the per-group MSE search over clipped max-abs
+    scales reproduces the reference's choice (and packing) bit for bit on
+    weights with planted outliers, where most groups pick a clipped scale."""
+    W = torch.from_numpy(golden[f"clip_g{G}_W"])
+    qw = ng.quantize(W, G, clip_search=True)
+    assert np.array_equal(qw.qweight.numpy(), golden[f"clip_g{G}_qweight"])
+    assert np.array_equal(qw.scales.numpy(), golden[f"clip_g{G}_scales"])
+    rtn = ng.quantize(W, G)
+    assert (rtn.scales.numpy() != golden[f"clip_g{G}_scales"]).mean() > 0.5

@@ -63,20 +63,20 @@ def test_3d_input_is_flattened_and_restored(shape):
 def test_bias_is_added_exactly():
     _, ql = make_layer(bias=True, seed=2)
     x = torch.randn(4, IN, device="cuda", dtype=torch.float16)
-    assert torch.equal(ql(x), ng.matmul(x, ql._qw()) + ql.bias)
+    assert torch.equal(ql(x), ng.matmul(x, ql.packed()) + ql.bias)
 
 
 def test_no_bias_is_a_plain_matmul():
     _, ql = make_layer(bias=False, seed=3)
     assert ql.bias is None
     x = torch.randn(4, IN, device="cuda", dtype=torch.float16)
-    assert torch.equal(ql(x), ng.matmul(x, ql._qw()))
+    assert torch.equal(ql(x), ng.matmul(x, ql.packed()))
 
 
 def test_from_linear_transposes_the_weight():
     linear, ql = make_layer(bias=False, seed=4)
     assert (ql.K, ql.N) == (IN, OUT)
-    approx = ng.dequant(ql._qw()).float().cpu()
+    approx = ng.dequant(ql.packed()).float().cpu()
     truth = linear.weight.data.t().float().cpu()
     assert (approx - truth).abs().mean() < 0.25 * truth.abs().mean()
 

@@ -20,6 +20,7 @@ import torch
 
 import nibblegemm_b200 as ng
 from nibblegemm_b200 import _lib
+from oracle import c_oracle
 from oracle import quant_oracle as qo
 
 pytestmark = pytest.mark.gpu
@@ -56,6 +57,10 @@ def test_noalloc_matches_regular_entry_point_twice(M, K, N, G, act):
         assert torch.isfinite(a).all(), f"call {call}"
         err = ((a - b).abs().max() / b.abs().max()).item()
         assert err <= GATE, (call, err)
+    # and against the CPU oracle directly, so a fault shared by both GPU paths shows
+    oracle = c_oracle.matmul_f32(x, q, s, G, K, x_kind=act)
+    y32 = y.float().cpu().numpy()
+    assert float(np.abs(y32 - oracle).max() / np.abs(oracle).max()) <= GATE
 
 
 def test_noalloc_rejects_bad_arguments():
