@@ -261,26 +261,51 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
 
 
+def cpu_model() -> str:
+    """The host CPU's model string (from /proc/cpuinfo), for the baseline record."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_reference_sample(wl, seconds: float = 12.0, threads: int = 0):
-    """Time the reference's CPU path (oracle port) on config shapes; returns
-    (GB/s in the same byte model, sample description, threads used)."""
+    """Time the reference's CPU path (the oracle port of quant.py's
+    reference_matmul: dequantise, then an fp32 matmul) on the workload shape:
+    the median of >= 5 full calls, and the steady state (weights dequantised
+    once, the fp32 matmul alone), bounded to about `seconds` in total.
+    Returns (GB/s of the full path, seconds per full call, sample text,
+    threads, extras dict)."""
     from oracle import quant_oracle as qo
     M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
     if threads > 0:
         torch.set_num_threads(threads)
     x, q, s = qo.synthetic_case(M, K, N, group_size=G, seed=1)
-    calls, t0 = 0, time.perf_counter()
-    while True:
-        W = qo.dequantize_np(q, s, G, K).astype(np.float32)
-        _ = (torch.from_numpy(x.astype(np.float32)) @ torch.from_numpy(W)).to(torch.float16)
-        calls += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or calls >= 50:
-            break
-    per = el / calls
-    return (algo_bytes(M, K, N, G) / per / 1e9, per,
-            f"{calls} full reference_matmul calls (numpy dequantise + torch fp32 matmul) at M={M} K={K} N={N}",
-            torch.get_num_threads())
+    xt = torch.from_numpy(x.astype(np.float32))
+    full, t_start = [], time.perf_counter()
+    while len(full) < 5 or (time.perf_counter() - t_start < seconds * 0.7 and len(full) < 50):
+        t0 = time.perf_counter()
+        W = torch.from_numpy(qo.dequantize_np(q, s, G, K).astype(np.float32))
+        _ = (xt @ W).to(torch.float16)
+        full.append(time.perf_counter() - t0)
+    steady = []
+    for _ in range(max(5, min(50, int(seconds * 0.3 / max(1e-4, min(full) / 4))))):
+        t0 = time.perf_counter()
+        _ = (xt @ W).to(torch.float16)
+        steady.append(time.perf_counter() - t0)
+    per = float(np.median(full))
+    per_mm = float(np.median(steady))
+    nbytes = algo_bytes(M, K, N, G)
+    extras = {"median_of": len(full), "steady_state_value": round(nbytes / per_mm / 1e9, 4),
+              "steady_state_ms_per_call": round(per_mm * 1e3, 3),
+              "steady_state_sample": f"median of {len(steady)} fp32 matmuls on pre-dequantised weights",
+              "cpu_model": cpu_model(), "os_cpu_count": os.cpu_count()}
+    return (nbytes / per / 1e9, per,
+            f"median of {len(full)} full reference_matmul calls (numpy dequantise + torch fp32 matmul) "
+            f"at M={M} K={K} N={N}", torch.get_num_threads(), extras)
 
 
 def run_reference_decode(args):
@@ -353,14 +378,15 @@ def run_reference(args, rank):
     # reports the steps actually timed.
     for _ in range(min(args.warmup, 3)):
         step()
-    t0, done = time.perf_counter(), 0
-    while done < args.steps:
+    t0, times = time.perf_counter(), []
+    while len(times) < args.steps:
+        t1 = time.perf_counter()
         step()
-        done += 1
-        if time.perf_counter() - t0 > 90.0:
+        times.append(time.perf_counter() - t1)
+        if time.perf_counter() - t0 > 90.0 and len(times) >= 5:
             break
-    el = time.perf_counter() - t0
-    per = el / done
+    done = len(times)
+    per = float(np.median(times))
     args.steps, args.warmup = done, min(args.warmup, 3)
     if args.workload == "gemv":
         value, unit = algo_bytes(M, K, N, G) / per / 1e9, "GB/s"
@@ -374,8 +400,8 @@ def run_reference(args, rank):
         "config": {"workload": wl["name"], "M": M, "K": K, "N": N, "group_size": G,
                    "l2": "n/a (host)"},
         "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"{args.steps} timed reference_matmul calls (numpy unpack + fp32 dequantise + torch fp32 matmul)"},
+                         "kind": "port", "cpu_model": cpu_model(), "os_cpu_count": os.cpu_count(),
+                         "sample": f"median of {args.steps} timed reference_matmul calls (numpy unpack + fp32 dequantise + torch fp32 matmul)"},
         "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -813,12 +839,13 @@ def main():
                 "timing": "device time of one CUDA-graph step, max over ranks; strong scaling (fixed model)",
             }
         if not args.no_cpu_baseline:
-            v, per, sample, cores = cpu_reference_sample(wl)
+            v, per, sample, cores, extras = cpu_reference_sample(wl)
             if args.workload == "gemm":
                 v = flops / per / 1e12
+                extras["steady_state_value"] = round(flops / (extras["steady_state_ms_per_call"] * 1e-3) / 1e12, 6)
             line["cpu_baseline"] = {"value": round(v, 6), "unit": unit,
                                     "cores": cores, "kind": "port", "sample": sample,
-                                    "ms_per_call": round(per * 1e3, 1)}
+                                    "ms_per_call": round(per * 1e3, 1), **extras}
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

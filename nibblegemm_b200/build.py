@@ -57,6 +57,29 @@ def _compile(src: str, force: bool, verbose: bool) -> str:
     return obj
 
 
+TORCH_EXT_NAME = "nibblegemm_b200_torch"
+TORCH_EXT_DIR = os.path.join(OBJ, "torchext")
+
+
+def build_torch_binding(verbose: bool = False) -> str:
+    """Compile ``csrc/torch_binding.cpp`` (the tensor-level ops over the C ABI)
+    into ``_build/torchext/nibblegemm_b200_torch*.so``, linked against the
+    library with an rpath to the package directory.  Host C++ only (no nvcc)."""
+    import torch.utils.cpp_extension as ext
+    os.makedirs(TORCH_EXT_DIR, exist_ok=True)
+    ext.load(name=TORCH_EXT_NAME, sources=[os.path.join(CSRC, "torch_binding.cpp")],
+             extra_include_paths=[INCLUDE], extra_cflags=["-O3", "-std=c++17"],
+             extra_ldflags=[f"-L{PKG}", "-lnibblegemm_b200", f"-Wl,-rpath,{PKG}"],
+             build_directory=TORCH_EXT_DIR, with_cuda=True, verbose=verbose, is_python_module=True)
+    return torch_binding_path()
+
+
+def torch_binding_path() -> str:
+    """Path of the built binding module (may not exist)."""
+    cands = sorted(glob.glob(os.path.join(TORCH_EXT_DIR, TORCH_EXT_NAME + "*.so")))
+    return cands[0] if cands else os.path.join(TORCH_EXT_DIR, TORCH_EXT_NAME + ".so")
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
@@ -78,3 +101,4 @@ if __name__ == "__main__":
     ap.add_argument("-v", "--verbose", action="store_true", help="print ptxas resource usage")
     a = ap.parse_args()
     print(build(a.force, a.verbose))
+    print(build_torch_binding(a.verbose))

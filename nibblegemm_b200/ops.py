@@ -98,11 +98,29 @@ def _out(out, M, N, X):
     return out
 
 
+def _load_binding():
+    """The compiled tensor-level binding (``csrc/torch_binding.cpp``), or None if
+    it has not been built (the ops then marshal through ctypes: same kernels,
+    more host time per call)."""
+    import importlib.machinery
+    import importlib.util
+    from .build import TORCH_EXT_NAME, torch_binding_path
+    path = torch_binding_path()
+    if not os.path.exists(path):
+        return None
+    loader = importlib.machinery.ExtensionFileLoader(TORCH_EXT_NAME, path)
+    spec = importlib.util.spec_from_loader(TORCH_EXT_NAME, loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
 class _Extension:
     """Tensor-level ops with the reference extension's signatures."""
 
     def __init__(self):
         self.lib = _lib.load()
+        self.binding = _load_binding()
         self._ws = {}  # (device index, stream handle) -> zero-initialised GEMV workspace
         self._gws = {}  # (device index, stream handle) -> zero-initialised GEMM split-K workspace
 
@@ -110,6 +128,8 @@ class _Extension:
         """The prefill-GEMM split-K workspace for (device, stream), grown on demand
         (zero-filled once; every call leaves its per-tile counters at zero)."""
         need = self.lib.ng_gemm_workspace_bytes(M, N)
+        if self.binding is not None:
+            return self.binding.workspace(device.index, stream, 1, need)
         key = (device.index, stream)
         ws = self._gws.get(key)
         if ws is None or ws.numel() < need:
@@ -125,6 +145,8 @@ class _Extension:
         stream, because calls sharing a workspace must not overlap on the GPU.
         """
         need = self.lib.ng_gemv_workspace_bytes(1, N)
+        if self.binding is not None:
+            return self.binding.workspace(device.index, stream, 0, need)
         key = (device.index, stream)
         ws = self._ws.get(key)
         if ws is None or ws.numel() < need:
@@ -134,6 +156,10 @@ class _Extension:
 
     def dequant_w4(self, Wq: torch.Tensor, S: torch.Tensor, group_size: int, fast: bool = True,
                    out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+        if self.binding is not None:
+            out = self.binding.dequant_w4(Wq, S, int(group_size), bool(fast), out_dtype)
+            _after("dequant_w4")
+            return out
         _check_weight(Wq, S, Wq.device)
         K, N = Wq.size(0) * 8, Wq.size(1)
         _require(S.size(1) == N, "scale columns disagree with N")
@@ -151,6 +177,11 @@ class _Extension:
     def gemv_w4a16(self, X: torch.Tensor, Wq: torch.Tensor, S: torch.Tensor, group_size: int,
                    version: int = 4, splits_override: int = 0, threads_override: int = 0,
                    algo: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.binding is not None:
+            y = self.binding.gemv_w4a16(X, Wq, S, int(group_size), int(version), int(splits_override),
+                                        int(threads_override), int(algo), out)
+            _after("gemv_w4a16")
+            return y
         M, K, N = _check_act(X, Wq, S, group_size)
         _require(N % 4 == 0, "N must be a multiple of 4 for 128-bit weight loads")
         _require(group_size in (64, 128, 256), "group_size must be 64, 128 or 256")
@@ -173,6 +204,10 @@ class _Extension:
     def gemm_w4a16(self, X: torch.Tensor, Wq: torch.Tensor, S: torch.Tensor, group_size: int,
                    version: int = 6, tile_tokens: int = 0,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.binding is not None:
+            y = self.binding.gemm_w4a16(X, Wq, S, int(group_size), int(version), int(tile_tokens), out)
+            _after("gemm_w4a16")
+            return y
         M, K, N = _check_act(X, Wq, S, group_size)
         _require(version in (6, 7), "version must be 6 or 7")
         y = _out(out, M, N, X)
