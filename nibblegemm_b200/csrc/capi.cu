@@ -67,7 +67,7 @@ void* tensor_map_encode_fn() {
 
 }  // namespace ngb
 
-extern "C" int ng_abi_version(void) { return 2; }
+extern "C" int ng_abi_version(void) { return 3; }
 
 extern "C" int ng_device_status(void* stream) {
   ngb::DeviceInfo dev;

@@ -4,8 +4,9 @@
 // guard, the current-stream lookup and the per-stream workspace cache done in
 // C++ -- a few microseconds per call instead of the tens a Python + ctypes path
 // costs.  The kernels are the ones of libnibblegemm_b200.so; this file only
-// marshals.  Check failures raise RuntimeError (TORCH_CHECK), as the
-// reference's do; a non-zero status from the library raises with its message.
+// marshals.  Argument-check failures raise RuntimeError (TORCH_CHECK), as the
+// reference's do; the library's own status is returned beside the output and
+// the Python wrapper raises on a non-zero one.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -23,10 +24,6 @@ int dtype_code(const torch::Tensor& t) {
   if (t.scalar_type() == torch::kHalf) return NG_DTYPE_F16;
   if (t.scalar_type() == torch::kBFloat16) return NG_DTYPE_BF16;
   TORCH_CHECK(false, "activations must be fp16 or bf16");
-}
-
-void check_status(int st, const char* what) {
-  TORCH_CHECK(st == NG_OK, what, ": ", ng_status_string(st), " (status ", st, ")");
 }
 
 void check_weight(const torch::Tensor& Wq, const torch::Tensor& S, const torch::Device& dev) {
@@ -81,7 +78,7 @@ torch::Tensor workspace(const torch::Device& dev, cudaStream_t stream, int kind,
   return ws;
 }
 
-torch::Tensor gemv_w4a16(torch::Tensor X, torch::Tensor Wq, torch::Tensor S, int64_t group_size,
+std::tuple<torch::Tensor, int64_t> gemv_w4a16(torch::Tensor X, torch::Tensor Wq, torch::Tensor S, int64_t group_size,
                          int64_t version, int64_t splits_override, int64_t threads_override,
                          int64_t algo, std::optional<torch::Tensor> out) {
   auto [M, K, N] = check_act(X, Wq, S, group_size);
@@ -96,16 +93,15 @@ torch::Tensor gemv_w4a16(torch::Tensor X, torch::Tensor Wq, torch::Tensor S, int
   auto Y = output(out, M, N, X);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.device().index()).stream();
   auto ws = workspace(X.device(), stream, 0, ng_gemv_workspace_bytes(1, static_cast<int>(N)));
-  check_status(ng_gemv_w4a16(X.data_ptr(), dtype_code(X), Wq.data_ptr<int32_t>(),
+  const int st = ng_gemv_w4a16(X.data_ptr(), dtype_code(X), Wq.data_ptr<int32_t>(),
                              reinterpret_cast<const uint16_t*>(S.data_ptr()), Y.data_ptr(),
                              static_cast<int>(M), static_cast<int>(K), static_cast<int>(N),
                              static_cast<int>(group_size), splits, static_cast<int>(threads_override),
-                             static_cast<int>(algo), ws.data_ptr(), static_cast<size_t>(ws.numel()), stream),
-               "gemv_w4a16");
-  return Y;
+                             static_cast<int>(algo), ws.data_ptr(), static_cast<size_t>(ws.numel()), stream);
+  return {Y, st};
 }
 
-torch::Tensor gemm_w4a16(torch::Tensor X, torch::Tensor Wq, torch::Tensor S, int64_t group_size,
+std::tuple<torch::Tensor, int64_t> gemm_w4a16(torch::Tensor X, torch::Tensor Wq, torch::Tensor S, int64_t group_size,
                          int64_t version, int64_t tile_tokens, std::optional<torch::Tensor> out) {
   auto [M, K, N] = check_act(X, Wq, S, group_size);
   TORCH_CHECK(version == 6 || version == 7, "version must be 6 or 7");
@@ -113,16 +109,15 @@ torch::Tensor gemm_w4a16(torch::Tensor X, torch::Tensor Wq, torch::Tensor S, int
   auto Y = output(out, M, N, X);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(X.device().index()).stream();
   auto ws = workspace(X.device(), stream, 1, ng_gemm_workspace_bytes(static_cast<int>(M), static_cast<int>(N)));
-  check_status(ng_gemm_w4a16(X.data_ptr(), dtype_code(X), Wq.data_ptr<int32_t>(),
+  const int st = ng_gemm_w4a16(X.data_ptr(), dtype_code(X), Wq.data_ptr<int32_t>(),
                              reinterpret_cast<const uint16_t*>(S.data_ptr()), Y.data_ptr(),
                              static_cast<int>(M), static_cast<int>(K), static_cast<int>(N),
                              static_cast<int>(group_size), static_cast<int>(tile_tokens), ws.data_ptr(),
-                             static_cast<size_t>(ws.numel()), stream),
-               "gemm_w4a16");
-  return Y;
+                             static_cast<size_t>(ws.numel()), stream);
+  return {Y, st};
 }
 
-torch::Tensor dequant_w4(torch::Tensor Wq, torch::Tensor S, int64_t group_size, bool fast,
+std::tuple<torch::Tensor, int64_t> dequant_w4(torch::Tensor Wq, torch::Tensor S, int64_t group_size, bool fast,
                          std::optional<torch::ScalarType> out_dtype) {
   check_weight(Wq, S, Wq.device());
   const int64_t K = Wq.size(0) * 8, N = Wq.size(1);
@@ -133,12 +128,11 @@ torch::Tensor dequant_w4(torch::Tensor Wq, torch::Tensor S, int64_t group_size, 
   const c10::cuda::CUDAGuard guard(Wq.device());
   auto out = torch::empty({K, N}, Wq.options().dtype(dt));
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(Wq.device().index()).stream();
-  check_status(ng_dequant_w4(Wq.data_ptr<int32_t>(), reinterpret_cast<const uint16_t*>(S.data_ptr()),
+  const int st = ng_dequant_w4(Wq.data_ptr<int32_t>(), reinterpret_cast<const uint16_t*>(S.data_ptr()),
                              out.data_ptr(), dt == torch::kHalf ? NG_DTYPE_F16 : NG_DTYPE_BF16,
                              static_cast<int>(K), static_cast<int>(N), static_cast<int>(group_size),
-                             fast ? 1 : 0, stream),
-               "dequant_w4");
-  return out;
+                             fast ? 1 : 0, stream);
+  return {out, st};
 }
 
 // The cached workspace a call on (device, stream) uses (for inspection).

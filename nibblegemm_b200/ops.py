@@ -157,7 +157,8 @@ class _Extension:
     def dequant_w4(self, Wq: torch.Tensor, S: torch.Tensor, group_size: int, fast: bool = True,
                    out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
         if self.binding is not None:
-            out = self.binding.dequant_w4(Wq, S, int(group_size), bool(fast), out_dtype)
+            out, st = self.binding.dequant_w4(Wq, S, int(group_size), bool(fast), out_dtype)
+            _lib.check(st, "dequant_w4")
             _after("dequant_w4")
             return out
         _check_weight(Wq, S, Wq.device)
@@ -178,8 +179,9 @@ class _Extension:
                    version: int = 4, splits_override: int = 0, threads_override: int = 0,
                    algo: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.binding is not None:
-            y = self.binding.gemv_w4a16(X, Wq, S, int(group_size), int(version), int(splits_override),
-                                        int(threads_override), int(algo), out)
+            y, st = self.binding.gemv_w4a16(X, Wq, S, int(group_size), int(version), int(splits_override),
+                                            int(threads_override), int(algo), out)
+            _lib.check(st, "gemv_w4a16")
             _after("gemv_w4a16")
             return y
         M, K, N = _check_act(X, Wq, S, group_size)
@@ -205,7 +207,8 @@ class _Extension:
                    version: int = 6, tile_tokens: int = 0,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.binding is not None:
-            y = self.binding.gemm_w4a16(X, Wq, S, int(group_size), int(version), int(tile_tokens), out)
+            y, st = self.binding.gemm_w4a16(X, Wq, S, int(group_size), int(version), int(tile_tokens), out)
+            _lib.check(st, "gemm_w4a16")
             _after("gemm_w4a16")
             return y
         M, K, N = _check_act(X, Wq, S, group_size)

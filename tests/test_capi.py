@@ -37,7 +37,7 @@ def status_codes():
 
 def test_library_builds_and_loads():
     lib = _lib.load()
-    assert lib.ng_abi_version() == 2
+    assert lib.ng_abi_version() == 3
 
 
 def test_every_declared_symbol_is_exported_and_bound():
