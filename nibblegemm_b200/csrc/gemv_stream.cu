@@ -1,16 +1,15 @@
 // Decode-regime fused dequant GEMV, bulk-copy tensor-pipe schedule (algo 6):
 // Y[M, N] = X[M, K] @ W for M <= 16, one launch.
 //
-// What sets the time (measured on B200, config 1 = 30.3 MB of weights): a GEMV
-// is one pass over the weights, so the kernel must keep most of them
-// requested at once and must let the next kernel on the stream start
-// requesting its own while this one drains.  Loads into registers cannot do
-// the first: at 64-128 registers per thread a lane holds 8-16 chunks, and the
-// grid that holds the whole matrix no longer fits one wave.  So the weights
-// come in by TMA into a shared-memory ring (a 32 KB stage is one instruction
-// per 8 KB box, no registers), the first stages are requested before
-// `griddepcontrol.wait`, and a CTA takes about half an SM (96 KB ring, 288
-// threads) so the next kernel's CTAs can become resident beside it.
+// What sets the time (measured on B200, config 1 = 30.3 MB of weights, CUDA
+// graph of back-to-back launches): 9.3 us per launch, the same as the ring
+// schedule (algo 5).  With the consumers' arithmetic compiled out the same
+// TMA pipeline reads config 1 in 6.2-6.8 us, so the consumers (decode + MMA at
+// about 0.5 IPC on the 112 SMs that 112 column tiles occupy) set the time,
+// not the copies.  Variants measured and not kept: deeper rings (4-6 stages),
+// 8 instead of 16 consumer warps (14.6 us), K split over clusters of 2-8 CTAs
+// (10.5-19.7 us), registers instead of a shared-memory ring (11-21 us), and a
+// stream-K grid over all 148 SMs (slower still, 21 us).
 //
 // Work decomposition (packed row = one int32 word = 8 values of K, one column)
 //   * CTA tile = 128 columns x a K slice of whole quantisation groups; the

@@ -143,6 +143,7 @@ int gemv_tc(const void* x, int x_dtype, const uint32_t* q, const __half* s, void
 // validated.  splits = cluster size (0 = heuristic).  Needs
 // gemv_stream_supported (N % 8 == 0, 16-byte aligned scales).
 bool gemv_stream_supported(int N, const void* scales);
+
 int gemv_stream(const void* x, int x_dtype, const uint32_t* q, const __half* s, void* y, int M,
                 int K, int N, int G, int splits, const DeviceInfo& dev, cudaStream_t strm);
 
