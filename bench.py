@@ -549,7 +549,7 @@ def run_step(args, wl, world, rank, local, dist):
     """
     import nibblegemm_b200 as ng
     from nibblegemm_b200.decode_step import LLAMA3_8B, ProjectionStackStep
-    step = ProjectionStackStep(LLAMA3_8B, batch=1, rank=rank, world=world, reduce=args.reduce)
+    step = ProjectionStackStep(LLAMA3_8B, batch=1, rank=rank, world=world, reduce=("peer" if args.reduce == "fused" else args.reduce))
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -642,8 +642,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp-decode", action="store_true",
                     help="gemv workload: skip the tensor-parallel Llama-3-8B decode-step measurement")
-    ap.add_argument("--reduce", choices=["peer", "nccl"], default="peer",
-                    help="tensor-parallel all-reduce of the step8b workload")
+    ap.add_argument("--reduce", choices=["peer", "nccl", "fused"], default="peer",
+                    help="tensor-parallel reduction: fused into the row-parallel GEMV (decode steps; the "
+                    "projection stack uses peer), the peer-memory all-reduce kernel, or NCCL")
     ap.add_argument("--batch", type=int, default=1, help="sequences per step (decode8b, decode70b)")
     ap.add_argument("--gemv-algo", type=int, default=None,
                     help="decode workloads: one ng_gemv_w4a16 algo for every projection")

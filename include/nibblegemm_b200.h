@@ -274,6 +274,28 @@ int ng_gemv_w4a16_silu(const void* gate_up, int x_dtype, const int32_t* qweight,
 int ng_gemv_w4a16_attn(const float* partials, int splits, int x_dtype, const int32_t* qweight,
                        const uint16_t* scales, void* y, int M, int K, int N, int group_size,
                        void* stream);
+/*
+ * Row-parallel projection fused with its tensor-parallel all-reduce (no
+ * counterpart in the reference, which runs on one GPU; replaces
+ * ng_gemv_w4a16 + ng_allreduce_sum after the o and down projections): every
+ * rank computes its K shard's partial Y with the cluster GEMV (algo 1 fp16 /
+ * 2 bf16), and each CTA exchanges its slice of the fp32 partials with the other
+ * ranks over NVLink peer memory inside the same kernel (plain stores, one flag
+ * per source, bounded waits) and sums them in rank order, so every rank gets
+ * the bit-identical full Y.
+ *   peer_buffers[p]: rank p's exchange buffer as mapped in this process (the
+ *   own one at index `rank`), ng_gemv_allreduce_buffer_bytes(world, N) bytes,
+ *   zero-filled before first use (ng_ipc_alloc / ng_ipc_open); one buffer per
+ *   (projection width, stream): calls sharing it must not overlap on the GPU.
+ *   stage_mode: 0 = X as given, 2 = X = silu(gate) * up from gate_up [M, 2K]
+ *   (as ng_gemv_w4a16_silu).  Every rank must call with the same shapes in the
+ *   same order.  M <= 16, world 2..8.  A peer that never arrives gives
+ *   NG_ERR_DEVICE_TIMEOUT in ng_device_status after 1 s (Y undefined).
+ */
+size_t ng_gemv_allreduce_buffer_bytes(int world, int N);
+int ng_gemv_w4a16_allreduce(const void* x, int x_dtype, const int32_t* qweight, const uint16_t* scales,
+                            void* y, int M, int K, int N, int group_size, int stage_mode,
+                            void* const* peer_buffers, int rank, int world, void* stream);
 /* Row-wise argmax of logits [M, V] (ties: smallest index): value[m] (fp32) and
  * index[m] + index_offset (int64; the offset places a vocab shard).
  * best_scratch: M x 8 bytes, zero before the first call; each call leaves it

@@ -47,6 +47,8 @@ SIGNATURES = {
     "ng_gemm_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
     "ng_gemv_w4a16_silu": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ng_gemv_w4a16_attn": (_I, [_P, _I, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "ng_gemv_allreduce_buffer_bytes": (ctypes.c_size_t, [_I, _I]),
+    "ng_gemv_w4a16_allreduce": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _I, _P]),
     "ng_lm_head_argmax": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_longlong, _P, _P, _P]),
     "ng_embed_tokens": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.c_longlong, _P, _P, _P]),
 }

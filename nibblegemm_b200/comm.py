@@ -19,6 +19,49 @@ from . import _lib
 _DT = {torch.float16: _lib.NG_DTYPE_F16, torch.bfloat16: _lib.NG_DTYPE_BF16}
 
 
+class PeerBuffers:
+    """One zero-filled exchange buffer per rank of a ``torch.distributed`` group on
+    one node, allocated by the library (``ng_ipc_alloc``), exported as a CUDA IPC
+    handle and mapped by every peer; ``ptrs`` is the ctypes array of every rank's
+    buffer as mapped in this process (this rank's own at index ``rank``)."""
+
+    def __init__(self, nbytes: int, group=None, device=None):
+        self.lib = _lib.load()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(self.device):
+            base, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+            _lib.check(self.lib.ng_ipc_alloc(int(nbytes), ctypes.byref(base), handle), "ng_ipc_alloc")
+        self._base = base.value
+        infos = [None] * self.world
+        dist.all_gather_object(infos, handle.raw, group=group)
+        self._opened, ptrs = [], []
+        for p, h in enumerate(infos):
+            if p == self.rank:
+                ptrs.append(self._base)
+                continue
+            out = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(self.lib.ng_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(out)),
+                           "ng_ipc_open")
+            self._opened.append(out.value)
+            ptrs.append(out.value)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)
+
+    def close(self):
+        """Unmap the peers' buffers, then free this rank's (call on every rank,
+        after a barrier, when nothing is in flight)."""
+        for p in self._opened:
+            self.lib.ng_ipc_close(p)
+        self._opened = []
+        if self._base:
+            self.lib.ng_ipc_free(self._base)
+            self._base = None
+
+
 class PeerAllReduce:
     def __init__(self, max_elems: int, group=None, device=None):
         self.lib = _lib.load()

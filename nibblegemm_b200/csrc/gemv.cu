@@ -87,6 +87,37 @@ enum Path { kHalf2 = 0, kFloat2 = 1 };
 //     part[m][h][s] = (max_s, sum_s, o_s[128]) combined in split order,
 //     sum_s w_s o_s[d] / sum_s w_s sum_s with w_s = exp(max_s - max), exactly as
 //     the standalone combine kernel (the attention output before `o`).
+constexpr int kArMaxWorld = 8;
+constexpr int kArMaxSlices = 16;  // cluster ranks (K slices) per column tile
+
+// Exchange buffer of the fused GEMV + all-reduce, per rank (sized for any M <= 16):
+//   data  fp32 [2 parity][world][tiles][16 x 128]   (each source rank's partial Y)
+//   flags u32  [2 parity][tiles][16 slices][world]  (call counter + 1 per source)
+//   ctr   u32  [tiles][16 slices]                   (this rank's call counter per slice)
+struct ArLayout {
+  size_t data, flags, ctr, total;
+  __host__ __device__ ArLayout(int world, int tiles) {
+    data = static_cast<size_t>(2) * world * tiles * 16 * 128 * 4;
+    flags = static_cast<size_t>(2) * tiles * kArMaxSlices * world * 4;
+    ctr = static_cast<size_t>(tiles) * kArMaxSlices * 4;
+    total = data + flags + ctr;
+  }
+};
+
+__device__ __forceinline__ unsigned int ar_ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ar_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void ar_st_release(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 enum StageMode { kStagePlain = 0, kStageNorm = 1, kStageSilu = 2, kStageAttn = 3 };
 
 struct NormArgs {
@@ -97,6 +128,12 @@ struct NormArgs {
   int mode = kStagePlain;
   const float* part = nullptr;  // kStageAttn: [M][K / 128][splits][2 + 128]
   int splits = 0;
+  // Fused tensor-parallel reduction (world > 1): every rank's buffer, as mapped
+  // in this process (layout: see gemv_ar_layout).
+  unsigned char* peers[kArMaxWorld] = {};
+  int ar_rank = 0;
+  int ar_world = 1;
+  unsigned int* ar_err = nullptr;  // device error word (bounded flag waits)
 };
 
 template <bool XBF16>
@@ -443,34 +480,98 @@ __global__ void __launch_bounds__(WARPS * 32)
     }
   };
 
+  const bool fused_ar = na.ar_world > 1;
+  float* vals = nullptr;  // this CTA's reduced outputs [e0, e1) (fused all-reduce only)
+  int e0 = 0, e1 = E, slice = 0;
   if (csize == 1) {
     for (int e = tid; e < E; e += WARPS * 32) {
       float v = 0.f;
 #pragma unroll 4
       for (int w = 0; w < WARPS; ++w) v += red[w * E + e];
+      if (fused_ar)
+        fin[e] = v;
+      else
+        store(e, v);
+    }
+    if (!fused_ar) return;
+    vals = fin;
+  } else {
+    for (int e = tid; e < E; e += WARPS * 32) {
+      float v = 0.f;
+#pragma unroll 4
+      for (int w = 0; w < WARPS; ++w) v += red[w * E + e];
+      fin[e] = v;
+    }
+    // ---- cluster reduction over K slices through DSMEM ---------------------------
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    slice = static_cast<int>(cluster.block_rank());
+    const int per = (E + csize - 1) / csize;
+    e0 = slice * per;
+    e1 = min(E, e0 + per);
+    for (int e = e0 + tid; e < e1; e += WARPS * 32) {
+      float v = 0.f;
+      for (int r = 0; r < csize; ++r) v += cluster.map_shared_rank(fin, r)[e];
+      if (fused_ar)
+        red[e - e0] = v;  // red is private to this CTA: peers read only fin
+      else
+        store(e, v);
+    }
+    cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+    if (!fused_ar) return;
+    vals = red;
+  }
+
+  // ---- fused tensor-parallel all-reduce of this CTA's outputs over peer memory ----
+  // Push the slice to every rank's buffer (plain stores), raise this rank's
+  // flag there, wait (bounded) for every rank's flag here, sum in rank order:
+  // every rank ends with bit-identical Y.  One counter per (tile, slice) makes
+  // calls capturable in a CUDA graph; parity double-buffers the slots (a slot
+  // is rewritten only after every peer has passed the next call's flags).
+  {
+    const int W = na.ar_world, me = na.ar_rank;
+    const int tiles = (N + kCols - 1) / kCols;
+    const ArLayout L(W, tiles);
+    const int tile = blockIdx.x;
+    unsigned char* own = na.peers[me];
+    unsigned int* ctr = reinterpret_cast<unsigned int*>(own + L.data + L.flags) + tile * kArMaxSlices + slice;
+    __shared__ unsigned int s_ep;
+    __syncthreads();
+    if (tid == 0) s_ep = *ctr;
+    __syncthreads();
+    const unsigned int ep = s_ep;
+    const int par = static_cast<int>(ep & 1u);
+    auto data = [&](unsigned char* base, int src) {
+      return reinterpret_cast<float*>(base) + ((static_cast<size_t>(par) * W + src) * tiles + tile) * 2048;
+    };
+    auto flag = [&](unsigned char* base, int src) {
+      return reinterpret_cast<unsigned int*>(base + L.data) +
+             ((static_cast<size_t>(par) * tiles + tile) * kArMaxSlices + slice) * W + src;
+    };
+    for (int e = e0 + tid; e < e1; e += WARPS * 32) {
+      const float v = vals[e - e0];
+      for (int p = 0; p < W; ++p) data(na.peers[p], me)[e] = v;
+    }
+    __syncthreads();  // every push before the release stores (release is cumulative)
+    if (tid < W) ar_st_release(flag(na.peers[tid], me), ep + 1);
+    if (tid < W) {
+      const unsigned int* f = flag(own, tid);
+      const uint64_t t0 = ar_timer_ns();
+      while (ar_ld_acquire(f) != ep + 1) {
+        if (ar_timer_ns() - t0 > 1000000000ull) {
+          atomicOr(na.ar_err, kErrWaitTimeout);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    for (int e = e0 + tid; e < e1; e += WARPS * 32) {
+      float v = 0.f;
+      for (int src = 0; src < W; ++src) v += __ldcg(data(own, src) + e);  // rank order
       store(e, v);
     }
-    return;
+    if (tid == 0) *ctr = ep + 1;
   }
-  for (int e = tid; e < E; e += WARPS * 32) {
-    float v = 0.f;
-#pragma unroll 4
-    for (int w = 0; w < WARPS; ++w) v += red[w * E + e];
-    fin[e] = v;
-  }
-  // ---- cluster reduction over K slices through DSMEM ---------------------------
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster.sync();
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int per = (E + csize - 1) / csize;
-  const int e0 = rank * per;
-  const int e1 = min(E, e0 + per);
-  for (int e = e0 + tid; e < e1; e += WARPS * 32) {
-    float v = 0.f;
-    for (int r = 0; r < csize; ++r) v += cluster.map_shared_rank(fin, r)[e];
-    store(e, v);
-  }
-  cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
 // ---------------------------------------------------------------------------
@@ -727,4 +828,41 @@ extern "C" int ng_gemv_w4a16_attn(const float* partials, int splits, int x_dtype
   if (x_dtype == NG_DTYPE_BF16)
     return dispatch_m<true, kFloat2, 8>(partials, q, s, y, M, K, N, group_size, 0, dev, strm, na);
   return dispatch_m<false, kHalf2, 8>(partials, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+}
+
+extern "C" size_t ng_gemv_allreduce_buffer_bytes(int world, int N) {
+  if (world < 2 || world > ngb::kArMaxWorld || N <= 0) return 0;
+  return ngb::ArLayout(world, (N + ngb::kCols - 1) / ngb::kCols).total;
+}
+
+extern "C" int ng_gemv_w4a16_allreduce(const void* x, int x_dtype, const int32_t* qweight,
+                                       const uint16_t* scales, void* y, int M, int K, int N, int group_size,
+                                       int stage_mode, void* const* peer_buffers, int rank, int world,
+                                       void* stream) {
+  using namespace ngb;
+  if (!x || !qweight || !scales || !y || !peer_buffers) return NG_ERR_NULL_POINTER;
+  if (x_dtype != NG_DTYPE_F16 && x_dtype != NG_DTYPE_BF16) return NG_ERR_BAD_DTYPE;
+  if (M < 1 || M > 16 || K <= 0 || K % 8 != 0 || N <= 0 || N % 4 != 0) return NG_ERR_BAD_SHAPE;
+  if (group_size != 64 && group_size != 128 && group_size != 256) return NG_ERR_BAD_SHAPE;
+  if (K % group_size != 0) return NG_ERR_BAD_SHAPE;
+  if (world < 2 || world > kArMaxWorld || rank < 0 || rank >= world) return NG_ERR_BAD_ARGUMENT;
+  if (stage_mode != kStagePlain && stage_mode != kStageSilu) return NG_ERR_BAD_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || !aligned(y, 2))
+    return NG_ERR_MISALIGNED;
+  for (int p = 0; p < world; ++p)
+    if (!peer_buffers[p] || !aligned(peer_buffers[p], 16)) return NG_ERR_MISALIGNED;
+  DeviceInfo dev;
+  if (int st = current_device_info(&dev)) return st;
+  NormArgs na;
+  na.mode = stage_mode;
+  for (int p = 0; p < world; ++p) na.peers[p] = static_cast<unsigned char*>(peer_buffers[p]);
+  na.ar_rank = rank;
+  na.ar_world = world;
+  na.ar_err = dev.err;
+  const auto* q = reinterpret_cast<const uint32_t*>(qweight);
+  const auto* s = reinterpret_cast<const __half*>(scales);
+  auto strm = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NG_DTYPE_BF16)
+    return dispatch_m<true, kFloat2, 8>(x, q, s, y, M, K, N, group_size, 0, dev, strm, na);
+  return dispatch_m<false, kHalf2, 8>(x, q, s, y, M, K, N, group_size, 0, dev, strm, na);
 }

@@ -155,9 +155,17 @@ class Llama3Decoder:
         self.attn_ws = torch.empty(self.ext.lib.ng_attn_workspace_bytes(B, hq, attn_splits),
                                    dtype=torch.uint8, device=dev)
         self._peer = None
-        if world > 1 and reduce == "peer":
+        self._fused = None  # (o buffers, down buffers) of the fused GEMV + all-reduce
+        self.reduce = reduce if world > 1 else None
+        if world > 1 and reduce in ("peer", "fused"):
             from .comm import PeerAllReduce
             self._peer = PeerAllReduce(B * H, device=dev)
+        if world > 1 and reduce == "fused":
+            # The row-parallel o / down projections reduce inside their GEMV (cluster
+            # schedule, up to 4 tokens); larger batches keep the separate all-reduce.
+            from .comm import PeerBuffers
+            nbytes = self.ext.lib.ng_gemv_allreduce_buffer_bytes(world, H)
+            self._fused = (PeerBuffers(nbytes, device=dev), PeerBuffers(nbytes, device=dev))
         self.weight_bytes = sum(w[k].weight_bytes for w in self.w for k in ("qkv", "o", "gu", "down"))
 
     # -- helpers ---------------------------------------------------------------
@@ -206,7 +214,8 @@ class Llama3Decoder:
         per_layer = 4 + 1 + (0 if self.fold_attn else 1) + (0 if self.fused_rope else 1) + \
             (0 if self.fold_silu else 1)
         norms = sum(1 for w in self.w for k in ("qkv", "gu") if not (self.fused_norm and not self._wide(w[k])))
-        peer = 2 * L if self._peer is not None else 0
+        fused = self._fused is not None and self.batch <= 4 and not self.fold_attn
+        peer = 2 * L if (self._peer is not None and not fused) else 0
         return L * per_layer + norms + peer + 1 + 1 + 1 + 1  # embed, final norm, head, token decode
 
     # -- the step ----------------------------------------------------------------
@@ -256,7 +265,14 @@ class Llama3Decoder:
                                               self.max_ctx, self.attn_splits, 1.0 / math.sqrt(D),
                                               self.attn_ws.data_ptr(), self.attn_ws.numel(),
                                               self._stream()), "attn_decode")
-            if self.fold_attn:  # o projection with the attention combine in its staging
+            fused_ar = self._fused is not None and B <= 4 and not self.fold_attn
+            if fused_ar:  # o projection + its tensor-parallel reduction, one kernel
+                wo = w["o"]
+                _lib.check(lib.ng_gemv_w4a16_allreduce(
+                    self.attn.data_ptr(), dt, wo.qweight.data_ptr(), wo.scales.data_ptr(), self.o.data_ptr(),
+                    B, wo.K, wo.N, wo.group_size, 0, self._fused[0].ptrs, self.rank, self.world,
+                    self._stream()), "gemv_w4a16_allreduce")
+            elif self.fold_attn:  # o projection with the attention combine in its staging
                 wo = w["o"]
                 _lib.check(lib.ng_gemv_w4a16_attn(self.attn_ws.data_ptr(), self.attn_splits, dt,
                                                   wo.qweight.data_ptr(), wo.scales.data_ptr(),
@@ -264,9 +280,20 @@ class Llama3Decoder:
                                                   self._stream()), "gemv_w4a16_attn")
             else:
                 self._gemv(self.attn, w["o"], self.o)
-            self._allreduce(self.o)
+            if not fused_ar:
+                self._allreduce(self.o)
             norm_proj(self.o, w["mlp_norm"], w["gu"], self.gu)
-            if self.fold_silu:  # down projection with SwiGLU in its staging
+            if fused_ar:  # down projection (SwiGLU folded in or not) + its reduction
+                wd = w["down"]
+                src = self.gu if self.fold_silu else self.act
+                if not self.fold_silu:
+                    _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
+                                               self._stream()), "silu_mul")
+                _lib.check(lib.ng_gemv_w4a16_allreduce(
+                    src.data_ptr(), dt, wd.qweight.data_ptr(), wd.scales.data_ptr(), self.down.data_ptr(),
+                    B, wd.K, wd.N, wd.group_size, 2 if self.fold_silu else 0, self._fused[1].ptrs, self.rank,
+                    self.world, self._stream()), "gemv_w4a16_allreduce")
+            elif self.fold_silu:  # down projection with SwiGLU in its staging
                 wd = w["down"]
                 _lib.check(lib.ng_gemv_w4a16_silu(self.gu.data_ptr(), dt, wd.qweight.data_ptr(),
                                                   wd.scales.data_ptr(), self.down.data_ptr(), B, wd.K,
@@ -275,7 +302,8 @@ class Llama3Decoder:
                 _lib.check(lib.ng_silu_mul(self.gu.data_ptr(), self.act.data_ptr(), dt, B, self.inter,
                                            self._stream()), "silu_mul")
                 self._gemv(self.act, w["down"], self.down)
-            self._allreduce(self.down)
+            if not fused_ar:
+                self._allreduce(self.down)
             delta = self.down
         self._norm(delta, res, self.final_norm, self.xn)
         # fp16 lm_head with the argmax fused into its epilogue (vocab shard per rank)

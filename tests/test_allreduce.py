@@ -136,3 +136,98 @@ def test_peer_allreduce(world):
     for rank, fails, status in results:
         assert not fails, (rank, fails[:5])
         assert status == 0, (rank, status)
+
+
+def _fused_worker(rank, world, port, q):
+    """ng_gemv_w4a16_allreduce against ng_gemv_w4a16 + an NCCL all-reduce of the
+    partials, and every rank's Y bit-identical, over several calls (graph too)."""
+    import ctypes
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        import nibblegemm_b200 as ng
+        from nibblegemm_b200 import _lib
+        from nibblegemm_b200.comm import PeerBuffers
+        lib = _lib.load()
+        fails = []
+        for (M, K, N, mode) in [(1, 14336, 4096, 0), (3, 4096, 4096, 0), (2, 1792, 4096, 2), (16, 1024, 1028, 0)]:
+            g = torch.Generator().manual_seed(K + N + M)
+            Kr = K // world
+            W = torch.randn(K, N, generator=g) * 0.02
+            qw = ng.quantize(W[rank * Kr:(rank + 1) * Kr].contiguous(), 128 if Kr % 128 == 0 else 64).to("cuda")
+            xin = torch.randn(M, (2 * K if mode == 2 else K), generator=g).half().cuda()
+            if mode == 2:  # gate | up of this rank's slice
+                x_full = torch.cat([xin[:, rank * Kr:(rank + 1) * Kr], xin[:, K + rank * Kr:K + (rank + 1) * Kr]], 1).contiguous()
+                act = torch.empty(M, Kr, dtype=torch.float16, device="cuda")
+                lib.ng_silu_mul(x_full.data_ptr(), act.data_ptr(), 0, M, Kr, torch.cuda.current_stream().cuda_stream)
+                x_gemv = act
+            else:
+                x_full = xin[:, rank * Kr:(rank + 1) * Kr].contiguous()
+                x_gemv = x_full
+            ref = ng.extension().gemv_w4a16(x_gemv, qw.qweight, qw.scales, qw.group_size, algo=1).float()
+            dist.all_reduce(ref)
+            bufs = PeerBuffers(lib.ng_gemv_allreduce_buffer_bytes(world, N))
+            for call in range(3):
+                y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+                st = lib.ng_gemv_w4a16_allreduce(x_full.data_ptr(), 0, qw.qweight.data_ptr(), qw.scales.data_ptr(),
+                                                 y.data_ptr(), M, Kr, N, qw.group_size, mode, bufs.ptrs, rank, world,
+                                                 torch.cuda.current_stream().cuda_stream)
+                if st != 0:
+                    fails.append(("status", M, K, N, st))
+                    break
+                torch.cuda.synchronize()
+                err = float((y.float() - ref).abs().max() / ref.abs().max())
+                if not err <= 5e-3:
+                    fails.append(("err", M, K, N, call, err))
+                allys = [torch.empty_like(y) for _ in range(world)]
+                dist.all_gather(allys, y)
+                if not all(torch.equal(a, allys[0]) for a in allys):
+                    fails.append(("ranks differ", M, K, N, call))
+            # CUDA-graph replays: the per-slice call counters live on the device
+            y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=s):
+                    lib.ng_gemv_w4a16_allreduce(x_full.data_ptr(), 0, qw.qweight.data_ptr(), qw.scales.data_ptr(),
+                                                y.data_ptr(), M, Kr, N, qw.group_size, mode, bufs.ptrs, rank,
+                                                world, s.cuda_stream)
+            torch.cuda.current_stream().wait_stream(s)
+            dist.barrier()
+            for _ in range(4):
+                gr.replay()
+                torch.cuda.synchronize()
+                err = float((y.float() - ref).abs().max() / ref.abs().max())
+                if not err <= 5e-3:
+                    fails.append(("graph err", M, K, N, err))
+            dist.barrier()
+            bufs.close()
+        status = ng.extension().device_status()
+        q.put((rank, fails, status))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, [repr(e)], -1))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_gemv_allreduce(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, 29823 + world, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, fails, status in results:
+        assert not fails, (rank, fails[:5])
+        assert status == 0, (rank, status)

@@ -143,13 +143,13 @@ def test_decoder_graph_replay_matches_eager_and_never_writes_past_the_cache():
     assert ng.extension().device_status() == 0
 
 
-def _tp_worker(rank, world, port, q):
+def _tp_worker(rank, world, port, q, reduce="peer"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        m = Llama3Decoder(TINY, batch=2, max_ctx=16, rank=rank, world=world, attn_splits=2)
+        m = Llama3Decoder(TINY, batch=2, max_ctx=16, rank=rank, world=world, attn_splits=2, reduce=reduce)
         toks = []
         for _ in range(5):
             m.step()
@@ -171,12 +171,14 @@ def _tp_worker(rank, world, port, q):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_decoder_tp_generates_the_tp1_tokens(world):
+@pytest.mark.parametrize("reduce", ["peer", "fused", "nccl"])
+def test_decoder_tp_generates_the_tp1_tokens(world, reduce):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_worker, args=(r, world, 29741 + world, q)) for r in range(world)]
+    port = 29741 + world + 10 * ["peer", "fused", "nccl"].index(reduce)
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q, reduce)) for r in range(world)]
     for p in procs:
         p.start()
     res = q.get(timeout=150)
