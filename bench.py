@@ -640,6 +640,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gemv")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true",
+                    help="gemv workload: skip the config-3 prefill GEMM point")
     ap.add_argument("--no-tp-decode", action="store_true",
                     help="gemv workload: skip the tensor-parallel Llama-3-8B decode-step measurement")
     ap.add_argument("--reduce", choices=["peer", "nccl", "fused"], default="peer",
@@ -793,8 +795,34 @@ def main():
                             reduce=args.reduce, local=local, sample_clocks=(rank == 0))
         assert tp["status"] == 0, "a decode-step kernel reported an error"
 
+    # ---- BASELINE config 3's headline point on this GPU: the prefill GEMM ----------
+    gemm_obj = None
+    if args.workload == "gemv" and not args.no_gemm:
+        gm = WORKLOADS["gemm"]
+        Mg, Kg, Ng, Gg = gm["M"], gm["K"], gm["N"], gm["G"]
+        xg, qg, sg = qo.synthetic_case(Mg, Kg, Ng, group_size=Gg, seed=5 + rank)
+        gw = [(torch.from_numpy(qg).cuda(), torch.from_numpy(sg).cuda()) for _ in range(8)]  # 8 x 30 MB
+        Xg = torch.from_numpy(xg).cuda()
+        Yg = torch.empty(Mg, Ng, dtype=torch.float16, device="cuda")
+        gsteps = max(10, min(args.steps, 50))
+        gop = lambda i: ext.gemm_w4a16(Xg, gw[i % 8][0], gw[i % 8][1], Gg, out=Yg)
+        gus = _graph_us(gop, gsteps, torch.cuda.Stream())
+        if dist:
+            t = torch.tensor([gus], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            gus = t.item()
+        gemm_obj = {"workload": gm["name"], "us_per_launch": round(gus, 2),
+                    "tflops": round(2.0 * Mg * Kg * Ng / (gus * 1e-6) / 1e12, 1),
+                    "timing": f"one CUDA graph of {gsteps} launches, weights rotated over 8 copies (240 MB > L2), "
+                              "device time, max over ranks"}
+        del gw, Xg, Yg
+
     if rank == 0:
         hbm, tf, src = measured_peaks()
+        if gemm_obj is not None:
+            gemm_obj["roofline"] = {"bound": "tensor", "achieved": gemm_obj["tflops"], "peak": tf,
+                                    "unit": "TFLOP/s", "frac": round(gemm_obj["tflops"] / tf, 4),
+                                    "peak_source": f"{src} cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops)"}
         if args.workload == "gemv":
             achieved = nbytes / (per_ms * 1e-3) / 1e9
             roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -826,6 +854,8 @@ def main():
             "clocks": clocks.summary(),
             "us_per_step": round(per_ms * 1e3, 3),
         }
+        if gemm_obj is not None:
+            line["prefill_gemm"] = gemm_obj
         if tp is not None:
             line["tp_decode8b"] = {
                 "metric": "Llama-3-8B INT4 g128 decode tokens/s (BASELINE config 4), batch 1, context 1024",

@@ -24,8 +24,11 @@ import torch
 from . import _lib
 from .quant import QuantizedWeight, quantize  # noqa: F401  (re-exported)
 
-#: Batch sizes at or below this go to the bandwidth-bound decode GEMV.
-DECODE_MAX_M = 8
+#: Batch sizes at or below this go to the bandwidth-bound decode GEMV.  The
+#: reference's crossover is 8 (ops.py:29-30); on B200 the GEMV stays ahead of the
+#: tcgen05 GEMM through M = 16 (4096 x 14336: 34.8 vs 38.9 us; 14336 x 4096:
+#: 26.4 vs 43.5 us, CUDA graph), and 16 is the largest M the GEMV takes.
+DECODE_MAX_M = 16
 
 _DTYPE_CODE = {torch.float16: _lib.NG_DTYPE_F16, torch.bfloat16: _lib.NG_DTYPE_BF16}
 

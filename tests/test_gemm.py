@@ -105,7 +105,7 @@ def test_deterministic_and_poisoned_output():
     assert ng.extension().device_status() == 0
 
 
-@pytest.mark.parametrize("M", [16, 64, 512])
+@pytest.mark.parametrize("M", [17, 64, 512])
 def test_matmul_dispatches_to_gemm_above_the_crossover(M):
     _, _, _, X, qw = make_case(M, 256, 128, 128, seed=1)
     assert M > ng.DECODE_MAX_M
