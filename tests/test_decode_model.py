@@ -149,14 +149,16 @@ def _tp_worker(rank, world, port, q, reduce="peer"):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        m = Llama3Decoder(TINY, batch=2, max_ctx=16, rank=rank, world=world, attn_splits=2, reduce=reduce)
+        # Key/value heads are sharded, not replicated: at least one per rank.
+        cfg = dict(TINY, kv_heads=max(TINY["kv_heads"], world))
+        m = Llama3Decoder(cfg, batch=2, max_ctx=16, rank=rank, world=world, attn_splits=2, reduce=reduce)
         toks = []
         for _ in range(5):
             m.step()
             torch.cuda.synchronize()
             toks.append(m.tokens.cpu())
         if rank == 0:
-            r = Llama3Decoder(TINY, batch=2, max_ctx=16, attn_splits=2)
+            r = Llama3Decoder(cfg, batch=2, max_ctx=16, attn_splits=2)
             ref = []
             for _ in range(5):
                 r.step()
