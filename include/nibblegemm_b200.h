@@ -233,6 +233,23 @@ int ng_rmsnorm(const void* x, void* residual, const void* weight, void* y, int d
 int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache, const int* pos,
                    int dtype, int M, int Hq, int Hkv, int D, float theta, int max_ctx,
                    void* stream);
+/* Prefill of B sequences of S prompt tokens each (token m = b * S + s of the
+ * [B * S, ...] activations, at position pos[b] + s; pos: device int array of B
+ * start positions).  No counterpart in the reference, which benchmarks the
+ * projections of a step only (bench/bench_model.py:43-86); these carry
+ * BASELINE config 5's 2048-token prefill around ng_gemm_w4a16.
+ *   ng_rope_prefill: ng_rope_append for runs of S consecutive positions per
+ *     sequence: q_out [B * S, Hq, D], K / V rows into the caches at pos[b] + s.
+ *   ng_attn_prefill: causal GQA attention, D = 128: query s of sequence b
+ *     attends to cache rows 0 .. pos[b] + s (inclusive; positions must stay
+ *     below max_ctx) -> out [B * S, Hq, D].  fp32 softmax, P rounded to the
+ *     activation type for the P V product. */
+int ng_rope_prefill(const void* qkv, void* q_out, void* k_cache, void* v_cache, const int* pos,
+                    int dtype, int B, int S, int Hq, int Hkv, int D, float theta, int max_ctx,
+                    void* stream);
+int ng_attn_prefill(const void* q, const void* k_cache, const void* v_cache, const int* pos, void* out,
+                    int dtype, int B, int S, int Hq, int Hkv, int D, int max_ctx, float scale,
+                    void* stream);
 size_t ng_attn_workspace_bytes(int M, int Hq, int splits);
 int ng_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int* ctx_len,
                    void* out, int dtype, int M, int Hq, int Hkv, int D, int max_ctx, int splits,

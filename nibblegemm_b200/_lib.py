@@ -29,6 +29,8 @@ SIGNATURES = {
     "ng_gemv_w4a16_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "ng_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _P]),
     "ng_rope_append": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P]),
+    "ng_rope_prefill": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P]),
+    "ng_attn_prefill": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P]),
     "ng_attn_workspace_bytes": (ctypes.c_size_t, [_I, _I, _I]),
     "ng_attn_decode": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P,
                             ctypes.c_size_t, _P]),

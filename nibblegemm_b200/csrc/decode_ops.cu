@@ -104,10 +104,13 @@ template <bool BF16>
 __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restrict__ q_out,
                                    void* __restrict__ k_cache, void* __restrict__ v_cache,
                                    const int* __restrict__ pos, int Hq, int Hkv, int D, float theta,
-                                   int max_ctx) {
+                                   int max_ctx, int T) {
   pdl_enter();
+  // Token m is number s = m % T of sequence seq = m / T, at position pos[seq] + s
+  // (decode: T = 1, one token per sequence; prefill: T tokens per sequence).
   const int m = blockIdx.y, head = blockIdx.x;  // head in [0, Hq + Hkv): q heads then k heads
-  const int p = pos[m];
+  const int seq = m / T;
+  const int p = pos[seq] + (m - seq * T);
   const bool in_cache = p >= 0 && p < max_ctx;  // cache rows outside [0, max_ctx) are never written
   if (head >= Hq && !in_cache) return;
   const int row = (Hq + 2 * Hkv) * D;
@@ -125,7 +128,7 @@ __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restric
       st_act<BF16>(q_out, dst + i + half, rb);
     } else {
       const int kh = head - Hq;
-      const size_t dst = ((static_cast<size_t>(m) * max_ctx + p) * Hkv + kh) * D;
+      const size_t dst = ((static_cast<size_t>(seq) * max_ctx + p) * Hkv + kh) * D;
       st_act<BF16>(k_cache, dst + i, ra);
       st_act<BF16>(k_cache, dst + i + half, rb);
     }
@@ -133,7 +136,7 @@ __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restric
   if (head >= Hq) {  // V rows: copied unrotated
     const int kh = head - Hq;
     const size_t vsrc = static_cast<size_t>(m) * row + static_cast<size_t>(Hq + Hkv + kh) * D;
-    const size_t dst = ((static_cast<size_t>(m) * max_ctx + p) * Hkv + kh) * D;
+    const size_t dst = ((static_cast<size_t>(seq) * max_ctx + p) * Hkv + kh) * D;
     for (int i = threadIdx.x; i < D; i += blockDim.x)
       static_cast<unsigned short*>(v_cache)[dst + i] = static_cast<const unsigned short*>(qkv)[vsrc + i];
   }
@@ -470,21 +473,38 @@ extern "C" int ng_rmsnorm(const void* x, void* residual, const void* weight, voi
     return launch_pdl(rmsnorm_kernel<false>, dim3(M), dim3(kNormThreads), st, x, residual, weight, y, H, eps);
 }
 
-extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache,
-                              const int* pos, int dtype, int M, int Hq, int Hkv, int D, float theta,
-                              int max_ctx, void* stream) {
+namespace {
+int rope_append_launch(const void* qkv, void* q_out, void* k_cache, void* v_cache, const int* pos,
+                       int dtype, int M, int T, int Hq, int Hkv, int D, float theta, int max_ctx,
+                       void* stream) {
   if (!qkv || !q_out || !k_cache || !v_cache || !pos) return NG_ERR_NULL_POINTER;
   if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
-  if (M < 1 || Hq < 1 || Hkv < 1 || D < 2 || D % 2 || Hq % Hkv || max_ctx < 1) return NG_ERR_BAD_SHAPE;
+  if (M < 1 || M > 65535 || T < 1 || M % T || Hq < 1 || Hkv < 1 || D < 2 || D % 2 || Hq % Hkv ||
+      max_ctx < 1)
+    return NG_ERR_BAD_SHAPE;
   auto st = static_cast<cudaStream_t>(stream);
   const dim3 grid(Hq + Hkv, M);
   if (dtype == NG_DTYPE_BF16)
-    return launch_pdl(rope_append_kernel<true>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
-                                                   max_ctx);
-  else
-    return launch_pdl(rope_append_kernel<false>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache, pos, Hq, Hkv, D, theta,
-                                                    max_ctx);
-  return launch_status();
+    return launch_pdl(rope_append_kernel<true>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache,
+                      pos, Hq, Hkv, D, theta, max_ctx, T);
+  return launch_pdl(rope_append_kernel<false>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache,
+                    pos, Hq, Hkv, D, theta, max_ctx, T);
+}
+}  // namespace
+
+extern "C" int ng_rope_append(const void* qkv, void* q_out, void* k_cache, void* v_cache,
+                              const int* pos, int dtype, int M, int Hq, int Hkv, int D, float theta,
+                              int max_ctx, void* stream) {
+  return rope_append_launch(qkv, q_out, k_cache, v_cache, pos, dtype, M, 1, Hq, Hkv, D, theta, max_ctx,
+                            stream);
+}
+
+extern "C" int ng_rope_prefill(const void* qkv, void* q_out, void* k_cache, void* v_cache,
+                               const int* pos, int dtype, int B, int S, int Hq, int Hkv, int D,
+                               float theta, int max_ctx, void* stream) {
+  if (B < 1 || S < 1) return NG_ERR_BAD_SHAPE;
+  return rope_append_launch(qkv, q_out, k_cache, v_cache, pos, dtype, B * S, S, Hq, Hkv, D, theta,
+                            max_ctx, stream);
 }
 
 extern "C" size_t ng_attn_workspace_bytes(int M, int Hq, int splits) {

@@ -29,7 +29,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .ops import extension
+from .ops import DECODE_MAX_M, extension
 from .quant import QuantizedWeight, quantize_on_device
 
 LLAMA3_8B_MODEL = dict(layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128,
@@ -217,6 +217,89 @@ class Llama3Decoder:
         fused = self._fused is not None and self.batch <= 4 and not self.fold_attn
         peer = 2 * L if (self._peer is not None and not fused) else 0
         return L * per_layer + norms + peer + 1 + 1 + 1 + 1  # embed, final norm, head, token decode
+
+    # -- prefill -----------------------------------------------------------------
+    def _prefill_buffers(self, S: int) -> dict:
+        """Activations of a prefill of S tokens per sequence (kept for reuse)."""
+        bufs = getattr(self, "_pf", None)
+        if bufs is not None and bufs["S"] == S:
+            return bufs
+        cfg, D, dev, dt = self.cfg, self.cfg["head_dim"], self.device, self.dtype
+        M, H = self.batch * S, cfg["hidden"]
+        e = lambda n: torch.empty(M, n, device=dev, dtype=dt)  # noqa: E731
+        self._pf = dict(S=S, res=e(H), xemb=e(H), xn=e(H), qkv=e((self.hq + 2 * self.hkv) * D),
+                        q=e(self.hq * D), attn=e(self.hq * D), o=e(H), gu=e(2 * self.inter),
+                        act=e(self.inter), down=e(H))
+        return self._pf
+
+    def _proj(self, x, w, out):
+        """A projection of a prefill: the tensor-core GEMM, or the GEMV for a few rows."""
+        if x.size(0) <= DECODE_MAX_M:
+            self.ext.gemv_w4a16(x, w.qweight, w.scales, w.group_size, out=out)
+        else:
+            self.ext.gemm_w4a16(x, w.qweight, w.scales, w.group_size, out=out)
+
+    def prefill(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Run the prompt ``tokens`` (int64 [batch, S] on the device) through the
+        model at positions ``self.pos + 0 .. S - 1`` of each sequence: every
+        projection as one [batch * S]-row tensor-core GEMM, RoPE + KV append for
+        the whole run, causal attention over the cache, and the head on each
+        sequence's last position.  Fills the KV caches, writes the next token of
+        each sequence into ``self.tokens`` (and the last position's logits into
+        ``self.logits``), advances ``self.pos`` by S and returns ``self.tokens``,
+        so ``step()`` continues the sequences."""
+        cfg, D, B = self.cfg, self.cfg["head_dim"], self.batch
+        if tokens.dim() != 2 or tokens.size(0) != B or tokens.dtype != torch.int64 or not tokens.is_cuda:
+            raise ValueError(f"tokens must be an int64 CUDA tensor [{B}, S]")
+        S = tokens.size(1)
+        tokens = tokens.contiguous()
+        lib, dt, st = self.ext.lib, _DT[self.dtype], self._stream()
+        H, M, eps = cfg["hidden"], B * S, float(cfg["eps"])
+        f = self._prefill_buffers(S)
+        _lib.check(lib.ng_embed_tokens(tokens.data_ptr(), None, None, self.embed.data_ptr(), dt, M, H,
+                                       cfg["vocab"], f["xemb"].data_ptr(), f["res"].data_ptr(), st),
+                   "embed_tokens")
+        delta, res = f["xemb"], f["res"]
+
+        def norm(x, w, y, rows=M):
+            _lib.check(lib.ng_rmsnorm(x.data_ptr(), res.data_ptr(), w.data_ptr(), y.data_ptr(), dt, rows,
+                                      H, eps, st), "rmsnorm")
+
+        for li, w in enumerate(self.w):
+            norm(delta, w["attn_norm"], f["xn"])
+            self._proj(f["xn"], w["qkv"], f["qkv"])
+            _lib.check(lib.ng_rope_prefill(f["qkv"].data_ptr(), f["q"].data_ptr(), self.k_cache[li].data_ptr(),
+                                           self.v_cache[li].data_ptr(), self.pos.data_ptr(), dt, B, S,
+                                           self.hq, self.hkv, D, float(cfg["rope_theta"]), self.max_ctx, st),
+                       "rope_prefill")
+            _lib.check(lib.ng_attn_prefill(f["q"].data_ptr(), self.k_cache[li].data_ptr(),
+                                           self.v_cache[li].data_ptr(), self.pos.data_ptr(), f["attn"].data_ptr(),
+                                           dt, B, S, self.hq, self.hkv, D, self.max_ctx, 1.0 / math.sqrt(D), st),
+                       "attn_prefill")
+            self._proj(f["attn"], w["o"], f["o"])
+            if self.world > 1:
+                torch.distributed.all_reduce(f["o"])
+            norm(f["o"], w["mlp_norm"], f["xn"])
+            self._proj(f["xn"], w["gu"], f["gu"])
+            _lib.check(lib.ng_silu_mul(f["gu"].data_ptr(), f["act"].data_ptr(), dt, M, self.inter, st), "silu_mul")
+            self._proj(f["act"], w["down"], f["down"])
+            if self.world > 1:
+                torch.distributed.all_reduce(f["down"])
+            delta = f["down"]
+        # the head reads each sequence's last position only
+        for b in range(B):
+            r = b * S + S - 1
+            _lib.check(lib.ng_rmsnorm(delta[r].data_ptr(), res[r].data_ptr(), self.final_norm.data_ptr(),
+                                      self.xn[b].data_ptr(), dt, 1, H, eps, st), "rmsnorm")
+        _lib.check(lib.ng_lm_head_argmax(self.xn.data_ptr(), self.lm_head.data_ptr(), dt, B, self.v1 - self.v0,
+                                         H, self.v0, self.logits.data_ptr() if self.keep_logits else None,
+                                         self.keys.data_ptr(), st), "lm_head_argmax")
+        if self.world > 1:
+            torch.distributed.all_reduce(self.keys, op=torch.distributed.ReduceOp.MAX)
+        _lib.check(lib.ng_embed_tokens(None, self.keys.data_ptr(), self.tokens.data_ptr(), self.embed.data_ptr(),
+                                       dt, B, H, cfg["vocab"], None, None, st), "embed_tokens")
+        self.pos.add_(S)
+        return self.tokens
 
     # -- the step ----------------------------------------------------------------
     def step(self, advance: bool = True) -> None:
