@@ -1,7 +1,8 @@
 """Benchmark of the W4A16 hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemv|gemm|step8b|decode8b|decode70b|readfloor|sweep2|sweep3]
+                    [--workload gemv|gemm|step8b|decode8b|decode70b|prefill8b|prefill70b|
+                                readfloor|sweep2|sweep3]
                     [--batch B] [--reduce peer|nccl] [--algo A] [--no-wide-split]
 
 Workload (default ``gemv``): BASELINE config 1 -- the decode GEMV
@@ -11,7 +12,8 @@ one fused dequant-GEMV over one batch.  ``--workload gemm`` times BASELINE
 config 3's M=2048, K=4096, N=14336 prefill GEMM instead (TFLOP/s).  The
 decode workloads (``step8b`` projection stack, ``decode8b`` / ``decode70b``
 full Llama-3 steps, tokens/s) replay one CUDA graph per token, tensor-parallel
-over torchrun ranks; ``readfloor``, ``sweep2`` and ``sweep3`` print one line
+over torchrun ranks; the prefill workloads (``prefill8b`` / ``prefill70b``)
+time ``Llama3Decoder.prefill`` of 2048 prompt tokens (prompt tokens/s); ``readfloor``, ``sweep2`` and ``sweep3`` print one line
 per measured point (diagnostics, not the headline).
 
 * ``value``: algorithmic bytes (``K*N/2 + K/G*N*2 + M*K*2 + M*N*2``, the
@@ -57,6 +59,8 @@ WORKLOADS = {
     "step8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 projection stack (224 projections), batch 1, tensor-parallel over the ranks"),
     "decode8b": dict(M=1, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 full decode step (BASELINE config 4): attention over a 1024-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch --batch (default 1), tensor-parallel over the ranks"),
     "decode70b": dict(M=1, K=8192, N=28672, G=128, name="Llama-3-70B INT4 g128 full decode step (BASELINE config 5): attention over a 2048-token KV cache, norms, RoPE, SwiGLU, fp16 lm_head + argmax, batch --batch, tensor-parallel over the ranks"),
+    "prefill70b": dict(M=2048, K=8192, N=28672, G=128, name="Llama-3-70B INT4 g128 prefill of 2048 synthetic token ids uniform over the vocab (BASELINE config 5): every projection a [batch x 2048]-row tcgen05 GEMM, causal GQA attention, norms, RoPE, SwiGLU, head on the last position, batch --batch, tensor-parallel over the ranks"),
+    "prefill8b": dict(M=2048, K=4096, N=14336, G=128, name="Llama-3-8B INT4 g128 prefill of 2048 synthetic token ids (config 4 model), as prefill70b"),
     "sweep2": dict(M=1, K=4096, N=14336, G=128, name="BASELINE config 2: decode GEMV sweep M x (K, N), eager and graph, vs cuBLAS fp16"),
     "readfloor": dict(M=1, K=4096, N=14336, G=128, name="transfer-size floor: config-1 GEMV at N x 1/2/4/8 beside a torch fp32 sum reading the same bytes"),
     "sweep3": dict(M=2048, K=4096, N=14336, G=128, name="BASELINE config 3: prefill GEMM sweep M x (K, N) x {fp16, bf16}"),
@@ -363,6 +367,8 @@ def run_reference(args, rank):
         return
     if args.workload in ("step8b", "decode8b", "decode70b"):
         return run_reference_decode(args)
+    if args.workload in ("prefill8b", "prefill70b"):
+        return run_reference_prefill(args)
     wl = WORKLOADS[args.workload]
     M, K, N, G = wl["M"], wl["K"], wl["N"], wl["G"]
     from oracle import quant_oracle as qo
@@ -539,6 +545,168 @@ def run_decode(args, wl, world, rank, local, dist):
         dist.destroy_process_group()
 
 
+PREFILL_TOKENS = 2048
+
+
+def prefill_flops(cfg, m, batch, S):
+    """FLOPs of one prefill on one rank: 2 per weight per token in the
+    projections, 4 * S^2 / 2 * D per (sequence, query head) in causal attention
+    (QK^T and PV), and the head on one position per sequence."""
+    proj = sum(w[k].K * w[k].N for w in m.w for k in ("qkv", "o", "gu", "down"))
+    attn = 2 * S * (S + 1) * cfg["head_dim"] * m.hq * cfg["layers"]
+    head = (m.v1 - m.v0) * cfg["hidden"]
+    return 2.0 * proj * batch * S + attn * batch + 2.0 * head * batch
+
+
+def run_prefill(args, wl, world, rank, local, dist):
+    """Prompt tokens/s of ``Llama3Decoder.prefill`` (the
+    Llama-3-70B prefill of 2048 synthetic token ids; ``prefill8b``: the 8B model).
+
+    One step = one prefill of 2048 tokens per sequence from position 0: the
+    embedding, then per layer RMSNorm, the q|k|v GEMM, RoPE + KV append for all
+    positions, causal GQA attention over the cache, the o GEMM (+ all-reduce),
+    RMSNorm, the gate|up GEMM, SwiGLU, the down GEMM (+ all-reduce), and the head
+    with its argmax on the last position.  Eager launches (each GEMM is
+    milliseconds long), CUDA events on the stream, max over ranks.  Strong
+    scaling: the same prompt, the model sharded over the ranks.
+    """
+    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL, Llama3Decoder
+    big = args.workload == "prefill70b"
+    cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
+    S, batch = PREFILL_TOKENS, args.batch
+    m = Llama3Decoder(cfg, batch=batch, max_ctx=S + 64, rank=rank, world=world, reduce="nccl")
+    g = torch.Generator().manual_seed(1234)
+    tok_host = torch.randint(0, cfg["vocab"], (batch, S), generator=g).pin_memory()
+    toks = tok_host.cuda()
+    out_host = torch.zeros(batch, dtype=torch.int64).pin_memory()
+
+    def one():
+        m.pos.zero_()
+        m.prefill(toks)
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        a.record()
+        for _ in range(args.steps):
+            one()
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    per_ms = ms / args.steps
+    # e2e: the prompt's ids from pinned host memory, the prefill, the next ids back
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    e_steps = max(1, min(args.steps, 5))
+    e0.record()
+    for _ in range(e_steps):
+        toks.copy_(tok_host, non_blocking=True)
+        one()
+        out_host.copy_(m.tokens, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    assert m.ext.device_status() == 0, "a kernel reported a bounded-wait timeout"
+    if rank == 0:
+        _, tf_burst, src = measured_peaks()
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if src == "measured" else {}
+        tf = peaks.get("bf16_tflops_sustained", tf_burst)  # a long step: the sustained figure
+        flops = prefill_flops(cfg, m, batch, S)
+        achieved = flops / (per_ms * 1e-3) / 1e12
+        L = cfg["layers"]
+        launches = 1 + 9 * L + batch + 2
+        line = {
+            "metric": METRIC, "value": round(1000.0 * batch * S / per_ms, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": f"synthetic random-init {'Llama-3-70B' if big else 'Llama-3-8B'} (seeded N(0,0.02) weights, RTN INT4 g128); prompt ids uniform over the vocab",
+            "config": {"workload": wl["name"], "layers": L, "hidden": cfg["hidden"], "heads": cfg["heads"],
+                       "kv_heads": cfg["kv_heads"], "intermediate": cfg["intermediate"], "vocab": cfg["vocab"],
+                       "prompt_tokens": S, "group_size": 128, "batch": batch, "parallelism": f"tp{world}",
+                       "tp_reduce": "nccl" if world > 1 else None,
+                       "l2": "every step streams all projection weights (>> L2)",
+                       "timing": "eager launches, CUDA events around `steps` prefills"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf, "unit": "TFLOP/s",
+                         "frac": round(achieved / tf, 4), "traffic": None,
+                         "peak_source": f"{src} cuBLAS bf16 (sustained: a step of {per_ms:.0f} ms)",
+                         "algorithmic_flops_per_step_per_rank": flops},
+            "e2e": {"value": round(1000.0 * batch * S / e2e_ms, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": 8 * batch * S, "d2h_bytes_per_step": 8 * batch,
+                    "path": "prompt ids in -> Llama3Decoder.prefill -> next ids out"},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del m
+    torch.cuda.empty_cache()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_reference_prefill(args):
+    """Reference arm of the prefill workloads: the reference's CPU path
+    (``reference_matmul``: numpy dequantise + torch fp32 matmul) for the 7
+    projection shapes of one layer on a bounded sample of 64 prompt rows,
+    scaled to the 2048-token prompt and the layer count.  Attention, norms and
+    the head are not counted, which favours the reference."""
+    from nibblegemm_b200.decode_step import LLAMA3_70B, LLAMA3_8B, layer_projections
+    from oracle import quant_oracle as qo
+    wl = WORKLOADS[args.workload]
+    cfg = LLAMA3_70B if args.workload == "prefill70b" else LLAMA3_8B
+    rows, batch = 64, args.batch
+    cases = []
+    for i, (_, K, N, _) in enumerate(layer_projections(cfg)):
+        x, q, s = qo.synthetic_case(rows, K, N, group_size=128, seed=i)
+        cases.append((torch.from_numpy(x.astype(np.float32)), q, s, K))
+
+    def step():
+        t = 0.0
+        for xt, q, s, K in cases:
+            t0 = time.perf_counter()
+            W = qo.dequantize_np(q, s, 128, K).astype(np.float32)
+            (xt @ torch.from_numpy(W)).to(torch.float16)
+            t += time.perf_counter() - t0
+        # one layer at `rows` prompt rows -> every layer at batch x 2048 rows
+        return t * (batch * PREFILL_TOKENS / rows) * cfg["layers"]
+
+    step()  # warm-up
+    t0, times = time.perf_counter(), []
+    while len(times) < max(1, min(args.steps, 5)):
+        times.append(step())
+        if time.perf_counter() - t0 > 90.0:
+            break
+    per = float(np.median(times))
+    value = batch * PREFILL_TOKENS / per
+    sample = (f"median of {len(times)} passes over the 7 projection shapes of one {args.workload} layer at "
+              f"{rows} prompt rows (reference_matmul each), scaled to {batch} x {PREFILL_TOKENS} tokens x "
+              f"{cfg['layers']} layers; projections only")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": 1, "ms_per_step": round(per * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (BASELINE distributions, seeded)",
+        "config": {"workload": wl["name"], "batch": batch, "prompt_tokens": PREFILL_TOKENS, "group_size": 128},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_step(args, wl, world, rank, local, dist):
     """Tokens/s of the Llama-3-8B INT4 projection stack.
 
@@ -682,6 +850,8 @@ def main():
         return run_step(args, wl, world, rank, local, dist)
     if args.workload in ("decode8b", "decode70b"):
         return run_decode(args, wl, world, rank, local, dist)
+    if args.workload in ("prefill8b", "prefill70b"):
+        return run_prefill(args, wl, world, rank, local, dist)
     if args.workload == "readfloor":
         if rank == 0:
             run_readfloor(args, local)

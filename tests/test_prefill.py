@@ -14,9 +14,11 @@ tensor-core GEMM over all prompt tokens, RoPE + KV append for the run
 from __future__ import annotations
 
 import math
+import os
 
 import pytest
 import torch
+import torch.multiprocessing as mp
 
 import nibblegemm_b200 as ng
 from nibblegemm_b200 import _lib
@@ -126,3 +128,50 @@ def test_prefill_then_decode_matches_decode_only(S):
         assert _rel(a.k_cache[li][:, :S + 3], b.k_cache[li][:, :S + 3].float()) <= 2e-2
     assert torch.equal(a.pos, b.pos)
     assert ng.extension().device_status() == 0
+
+
+def _tp_prefill_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        cfg = dict(TINY, kv_heads=max(TINY["kv_heads"], world))  # one key/value head per rank at least
+        toks = torch.randint(0, cfg["vocab"], (2, 40), generator=torch.Generator().manual_seed(3)).cuda()
+        m = Llama3Decoder(cfg, batch=2, max_ctx=48, rank=rank, world=world, attn_splits=2, reduce="nccl")
+        out = [m.prefill(toks).cpu().tolist()]
+        for _ in range(3):
+            m.step()
+            out.append(m.tokens.cpu().tolist())
+        torch.cuda.synchronize()
+        if rank == 0:
+            r = Llama3Decoder(cfg, batch=2, max_ctx=48, attn_splits=2)
+            ref = [r.prefill(toks).cpu().tolist()]
+            for _ in range(3):
+                r.step()
+                ref.append(r.tokens.cpu().tolist())
+            q.put({"tp": out, "tp1": ref})
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put({"worker error": repr(e)})
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_prefill_then_decode_generates_the_tp1_tokens(world):
+    """Megatron-sharded prefill (column-parallel q|k|v, gate|up; row-parallel
+    o, down with an NCCL all-reduce of the [batch x S, hidden] partials) and
+    the decode steps after it give the TP = 1 tokens."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_prefill_worker, args=(r, world, 29811 + world, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=150)
+    for p in procs:
+        p.join(timeout=60)
+    assert "worker error" not in res, res
+    assert res["tp"] == res["tp1"]
