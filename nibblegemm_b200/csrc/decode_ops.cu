@@ -142,6 +142,84 @@ __global__ void rope_append_kernel(const void* __restrict__ qkv, void* __restric
   }
 }
 
+// The same operation with one CTA per token, for D % 8 == 0 and D <= 256 (the
+// prefill case: thousands of tokens).  The D/2 angles' sines and cosines are
+// computed once per token into shared memory and shared by all of its heads;
+// each thread then rotates 4 consecutive pairs of one head with 8-byte loads
+// and stores, and the V rows are copied 16 bytes at a time.
+template <bool BF16>
+__device__ __forceinline__ void st_act4(void* p, size_t i, const float (&f)[4]) {
+  uint32_t w[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    if constexpr (BF16) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+      const __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  }
+  *reinterpret_cast<uint2*>(static_cast<unsigned short*>(p) + i) = make_uint2(w[0], w[1]);
+}
+
+constexpr int kRopeTokThreads = 256;
+
+template <bool BF16>
+__global__ void __launch_bounds__(kRopeTokThreads)
+    rope_append_tok_kernel(const void* __restrict__ qkv, void* __restrict__ q_out,
+                           void* __restrict__ k_cache, void* __restrict__ v_cache,
+                           const int* __restrict__ pos, int Hq, int Hkv, int D, float theta,
+                           int max_ctx, int T) {
+  __shared__ float cs[128], sn[128];
+  pdl_enter();
+  const int m = blockIdx.x;
+  const int seq = m / T;
+  const int p = pos[seq] + (m - seq * T);
+  const bool in_cache = p >= 0 && p < max_ctx;  // cache rows outside [0, max_ctx) are never written
+  const int half = D / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float inv_freq = exp2f(-2.f * i / D * log2f(theta));
+    sincosf(static_cast<float>(p) * inv_freq, &sn[i], &cs[i]);
+  }
+  __syncthreads();
+  const int row = (Hq + 2 * Hkv) * D;
+  const int q4 = half / 4;                       // 4-pair chunks per head
+  const int heads = in_cache ? Hq + Hkv : Hq;    // K heads only when the row is stored
+  for (int it = threadIdx.x; it < heads * q4; it += blockDim.x) {
+    const int head = it / q4, i = (it - head * q4) * 4;
+    const size_t src = static_cast<size_t>(m) * row + static_cast<size_t>(head) * D;
+    float a[4], b[4], ra[4], rb[4];
+    ld_act4<BF16>(qkv, src + i, a);
+    ld_act4<BF16>(qkv, src + i + half, b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ra[j] = a[j] * cs[i + j] - b[j] * sn[i + j];
+      rb[j] = b[j] * cs[i + j] + a[j] * sn[i + j];
+    }
+    size_t dst;
+    void* base;
+    if (head < Hq) {
+      dst = (static_cast<size_t>(m) * Hq + head) * D;
+      base = q_out;
+    } else {
+      dst = ((static_cast<size_t>(seq) * max_ctx + p) * Hkv + (head - Hq)) * D;
+      base = k_cache;
+    }
+    st_act4<BF16>(base, dst + i, ra);
+    st_act4<BF16>(base, dst + i + half, rb);
+  }
+  if (!in_cache) return;
+  const int c8 = D / 8;  // V rows: copied unrotated, 16 bytes at a time
+  for (int it = threadIdx.x; it < Hkv * c8; it += blockDim.x) {
+    const int kh = it / c8, c = it - kh * c8;
+    const size_t vsrc = static_cast<size_t>(m) * row + static_cast<size_t>(Hq + Hkv + kh) * D + 8 * c;
+    const size_t dst = ((static_cast<size_t>(seq) * max_ctx + p) * Hkv + kh) * D + 8 * c;
+    *reinterpret_cast<uint4*>(static_cast<unsigned short*>(v_cache) + dst) =
+        *reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(qkv) + vsrc);
+  }
+}
+
 // Split-context GQA decode attention, D = 128.  Grid (Hkv, splits, M): a CTA
 // owns one KV head, one contiguous chunk of the context and one token; its
 // G = Hq / Hkv warps are the query heads sharing that KV head (lane l holds
@@ -479,10 +557,20 @@ int rope_append_launch(const void* qkv, void* q_out, void* k_cache, void* v_cach
                        void* stream) {
   if (!qkv || !q_out || !k_cache || !v_cache || !pos) return NG_ERR_NULL_POINTER;
   if (!dtype_ok(dtype)) return NG_ERR_BAD_DTYPE;
-  if (M < 1 || M > 65535 || T < 1 || M % T || Hq < 1 || Hkv < 1 || D < 2 || D % 2 || Hq % Hkv ||
+  if (M < 1 || T < 1 || M % T || (T == 1 && M > 65535) || Hq < 1 || Hkv < 1 || D < 2 || D % 2 || Hq % Hkv ||
       max_ctx < 1)
     return NG_ERR_BAD_SHAPE;
   auto st = static_cast<cudaStream_t>(stream);
+  const bool vec = D % 8 == 0 && D <= 256 && aligned(qkv, 16) && aligned(q_out, 8) &&
+                   aligned(k_cache, 16) && aligned(v_cache, 16);
+  if (vec && T > 1) {  // many tokens: one CTA per token
+    if (dtype == NG_DTYPE_BF16)
+      return launch_pdl(rope_append_tok_kernel<true>, dim3(M), dim3(kRopeTokThreads), st, qkv, q_out,
+                        k_cache, v_cache, pos, Hq, Hkv, D, theta, max_ctx, T);
+    return launch_pdl(rope_append_tok_kernel<false>, dim3(M), dim3(kRopeTokThreads), st, qkv, q_out,
+                      k_cache, v_cache, pos, Hq, Hkv, D, theta, max_ctx, T);
+  }
+  if (M > 65535) return NG_ERR_BAD_SHAPE;  // the per-head grid's y extent
   const dim3 grid(Hq + Hkv, M);
   if (dtype == NG_DTYPE_BF16)
     return launch_pdl(rope_append_kernel<true>, dim3(grid), dim3(64), st, qkv, q_out, k_cache, v_cache,
