@@ -33,7 +33,10 @@ per measured point (diagnostics, not the headline).
   reference arm (rank 0 only under torchrun).
 
 Multi-GPU: the GEMV does not shard -- ranks run independent replicas (weak
-scaling, no collective on the data path).
+scaling, no collective on the data path).  The default line also carries the
+sharded paths measured over all ranks of the run (strong scaling):
+``tp_decode8b`` (the Llama-3-8B decode step) and ``tp_prefill70b`` (config 5's
+Llama-3-70B prefill of 2048 tokens).
 """
 from __future__ import annotations
 
@@ -558,22 +561,12 @@ def prefill_flops(cfg, m, batch, S):
     return 2.0 * proj * batch * S + attn * batch + 2.0 * head * batch
 
 
-def run_prefill(args, wl, world, rank, local, dist):
-    """Prompt tokens/s of ``Llama3Decoder.prefill`` (BASELINE config 5: the
-    Llama-3-70B prefill of 2048 synthetic token ids; ``prefill8b``: the 8B model).
-
-    One step = one prefill of 2048 tokens per sequence from position 0: the
-    embedding, then per layer RMSNorm, the q|k|v GEMM, RoPE + KV append for all
-    positions, causal GQA attention over the cache, the o GEMM (+ all-reduce),
-    RMSNorm, the gate|up GEMM, SwiGLU, the down GEMM (+ all-reduce), and the head
-    with its argmax on the last position.  Eager launches (each GEMM is
-    milliseconds long), CUDA events on the stream, max over ranks.  Strong
-    scaling: the same prompt, the model sharded over the ranks.
-    """
-    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL, Llama3Decoder
-    big = args.workload == "prefill70b"
-    cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
-    S, batch = PREFILL_TOKENS, args.batch
+def measure_prefill(cfg, batch, steps, warmup, world, rank, dist, local=0, sample_clocks=True):
+    """Device-timed prefill of PREFILL_TOKENS prompt tokens per sequence
+    (every rank runs its tensor-parallel shard), plus the end-to-end figure
+    with the prompt ids crossing PCIe.  Returns raw figures (same on every rank)."""
+    from nibblegemm_b200.decode_model import Llama3Decoder
+    S = PREFILL_TOKENS
     m = Llama3Decoder(cfg, batch=batch, max_ctx=S + 64, rank=rank, world=world, reduce="nccl")
     g = torch.Generator().manual_seed(1234)
     tok_host = torch.randint(0, cfg["vocab"], (batch, S), generator=g).pin_memory()
@@ -584,15 +577,16 @@ def run_prefill(args, wl, world, rank, local, dist):
         m.pos.zero_()
         m.prefill(toks)
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         one()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    sampler = ClockSampler(local) if sample_clocks else contextlib.nullcontext()
+    with sampler as clocks:
         a.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             one()
         b.record()
         torch.cuda.synchronize()
@@ -601,12 +595,12 @@ def run_prefill(args, wl, world, rank, local, dist):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
-    per_ms = ms / args.steps
+    per_ms = ms / steps
     # e2e: the prompt's ids from pinned host memory, the prefill, the next ids back
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
-    e_steps = max(1, min(args.steps, 5))
+    e_steps = max(1, min(steps, 5))
     e0.record()
     for _ in range(e_steps):
         toks.copy_(tok_host, non_blocking=True)
@@ -620,15 +614,43 @@ def run_prefill(args, wl, world, rank, local, dist):
         t = torch.tensor([e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = t.item()
-    assert m.ext.device_status() == 0, "a kernel reported a bounded-wait timeout"
+    out = dict(per_ms=per_ms, e2e_ms=e2e_ms, flops=prefill_flops(cfg, m, batch, S),
+               launches=1 + 9 * cfg["layers"] + batch + 2, status=m.ext.device_status(),
+               clocks=clocks.summary() if sample_clocks else None)
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
+def sustained_tflops():
+    _, tf_burst, src = measured_peaks()
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if src == "measured" else {}
+    return peaks.get("bf16_tflops_sustained", tf_burst), src
+
+
+def run_prefill(args, wl, world, rank, local, dist):
+    """Prompt tokens/s of ``Llama3Decoder.prefill`` (BASELINE config 5: the
+    Llama-3-70B prefill of 2048 synthetic token ids; ``prefill8b``: the 8B model).
+
+    One step = one prefill of 2048 tokens per sequence from position 0: the
+    embedding, then per layer RMSNorm, the q|k|v GEMM, RoPE + KV append for all
+    positions, causal GQA attention over the cache, the o GEMM (+ all-reduce),
+    RMSNorm, the gate|up GEMM, SwiGLU, the down GEMM (+ all-reduce), and the head
+    with its argmax on the last position.  Eager launches (each GEMM is
+    milliseconds long), CUDA events on the stream, max over ranks.  Strong
+    scaling: the same prompt, the model sharded over the ranks.
+    """
+    from nibblegemm_b200.decode_model import LLAMA3_8B_MODEL, LLAMA3_70B_MODEL
+    big = args.workload == "prefill70b"
+    cfg = LLAMA3_70B_MODEL if big else LLAMA3_8B_MODEL
+    S, batch = PREFILL_TOKENS, args.batch
+    r = measure_prefill(cfg, batch, args.steps, args.warmup, world, rank, dist, local)
+    assert r["status"] == 0, "a kernel reported a bounded-wait timeout"
     if rank == 0:
-        _, tf_burst, src = measured_peaks()
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if src == "measured" else {}
-        tf = peaks.get("bf16_tflops_sustained", tf_burst)  # a long step: the sustained figure
-        flops = prefill_flops(cfg, m, batch, S)
+        tf, src = sustained_tflops()
+        per_ms, flops = r["per_ms"], r["flops"]
         achieved = flops / (per_ms * 1e-3) / 1e12
         L = cfg["layers"]
-        launches = 1 + 9 * L + batch + 2
         line = {
             "metric": METRIC, "value": round(1000.0 * batch * S / per_ms, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 3),
@@ -644,15 +666,13 @@ def run_prefill(args, wl, world, rank, local, dist):
                          "frac": round(achieved / tf, 4), "traffic": None,
                          "peak_source": f"{src} cuBLAS bf16 (sustained: a step of {per_ms:.0f} ms)",
                          "algorithmic_flops_per_step_per_rank": flops},
-            "e2e": {"value": round(1000.0 * batch * S / e2e_ms, 1), "unit": "tok/s",
+            "e2e": {"value": round(1000.0 * batch * S / r["e2e_ms"], 1), "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * batch * S, "d2h_bytes_per_step": 8 * batch,
                     "path": "prompt ids in -> Llama3Decoder.prefill -> next ids out"},
-            "gpu_launches": launches * args.steps,
-            "clocks": clocks.summary(),
+            "gpu_launches": r["launches"] * args.steps,
+            "clocks": r["clocks"],
         }
         print(json.dumps(line), flush=True)
-    del m
-    torch.cuda.empty_cache()
     if dist:
         dist.destroy_process_group()
 
@@ -810,6 +830,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true",
                     help="gemv workload: skip the config-3 prefill GEMM point")
+    ap.add_argument("--no-tp-prefill", action="store_true",
+                    help="default workload: skip the tensor-parallel Llama-3-70B prefill object")
     ap.add_argument("--no-tp-decode", action="store_true",
                     help="gemv workload: skip the tensor-parallel Llama-3-8B decode-step measurement")
     ap.add_argument("--reduce", choices=["peer", "nccl", "fused"], default="peer",
@@ -965,6 +987,13 @@ def main():
                             reduce=args.reduce, local=local, sample_clocks=(rank == 0))
         assert tp["status"] == 0, "a decode-step kernel reported an error"
 
+    # ---- config 5's prefill at this N: Llama-3-70B, 2048 prompt tokens, tensor-parallel ----
+    tpp = None
+    if args.workload == "gemv" and not args.no_tp_prefill:
+        from nibblegemm_b200.decode_model import LLAMA3_70B_MODEL
+        tpp = measure_prefill(LLAMA3_70B_MODEL, 1, 3, 2, world, rank, dist, local, sample_clocks=(rank == 0))
+        assert tpp["status"] == 0, "a prefill kernel reported an error"
+
     # ---- BASELINE config 3's headline point on this GPU: the prefill GEMM ----------
     gemm_obj = None
     if args.workload == "gemv" and not args.no_gemm:
@@ -1038,6 +1067,21 @@ def main():
                                       "frac": round(tp["nbytes"] / (tp["per_ms"] * 1e-3) / 1e9 / hbm, 4)},
                 "gpu_launches_per_token": tp["launches"], "clocks": tp["clocks"],
                 "timing": "device time of one CUDA-graph step, max over ranks; strong scaling (fixed model)",
+            }
+        if tpp is not None:
+            tf, src = sustained_tflops()
+            ach = tpp["flops"] / (tpp["per_ms"] * 1e-3) / 1e12
+            line["tp_prefill70b"] = {
+                "metric": "Llama-3-70B INT4 g128 prefill of 2048 prompt tokens (BASELINE config 5), batch 1",
+                "value": round(1000.0 * PREFILL_TOKENS / tpp["per_ms"], 1), "unit": "tok/s", "world": world,
+                "parallelism": f"tp{world}", "reduce": "nccl" if world > 1 else None,
+                "ms_per_prefill": round(tpp["per_ms"], 3),
+                "e2e_tok_s": round(1000.0 * PREFILL_TOKENS / tpp["e2e_ms"], 1),
+                "roofline_per_rank": {"bound": "tensor", "algorithmic_flops": tpp["flops"],
+                                      "achieved_tflops": round(ach, 1), "peak": tf, "frac": round(ach / tf, 4),
+                                      "peak_source": f"{src} cuBLAS bf16 sustained"},
+                "gpu_launches_per_prefill": tpp["launches"], "clocks": tpp["clocks"],
+                "timing": "device time of 3 eager prefills after 2 warm-up, max over ranks; strong scaling (fixed model)",
             }
         if not args.no_cpu_baseline:
             v, per, sample, cores, extras = cpu_reference_sample(wl)
