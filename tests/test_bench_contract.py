@@ -52,3 +52,18 @@ def test_reference_arm_decode_workload_reports_tokens_per_second():
     assert d["impl"] == "reference" and d["unit"] == "tok/s" and d["value"] > 0
     assert d["warmup"] >= 3 and d["cpu_baseline"]["unit"] == "tok/s"
     assert d["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_reference_arm_prefill_workload_reports_prompt_tokens_per_second():
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "prefill8b",
+                          "--steps", "1", "--warmup", "3"], cwd=ROOT, env=dict(os.environ),
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["unit"] == "tok/s" and d["value"] > 0
+    assert d["config"]["prompt_tokens"] == 2048 and d["scaling"] == "strong"
+    assert d["cpu_baseline"]["kind"] == "port" and "scaled to" in d["cpu_baseline"]["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
